@@ -1,0 +1,83 @@
+"""B200-native (sm_100a) Kimi Delta Attention core.
+
+Drop-in replacement for the two kernels of Lazy-Hakimi/-kimi-linear-:
+``kimi_linear.kda.kda_chunkwise`` (``kimi_linear/kda.py:58-185``) and
+``kimi_linear.kda.kda_recurrent`` (``kimi_linear/kda.py:188-219``), backed by
+hand-written CUDA kernels behind the C ABI of ``include/kda_b200.h``.
+
+The directory name is not a Python identifier, so import it with
+``importlib.import_module("-kimi-linear-_b200")``; the package then also
+registers itself (and its submodules) as ``kimi_linear_b200``.
+
+To route an existing ``kimi_linear`` model through these kernels::
+
+    import importlib
+    kb = importlib.import_module("-kimi-linear-_b200")
+    kb.install()            # patches kimi_linear.kda.* and the package re-exports
+
+``KimiDeltaAttention.forward`` looks the two functions up as module globals at
+call time (``kda.py:503,519,526``), so prefill, eager decode and
+``GraphedDecoder`` all take the new path without further changes.
+"""
+
+from __future__ import annotations
+
+import sys as _sys
+
+from . import _lib, ops, synth
+from ._lib import KdaLibraryError
+from .ops import KdaError, chunkwise_path, kda_chunkwise, kda_recurrent
+
+ALIAS = "kimi_linear_b200"
+if __name__ != ALIAS:
+    _sys.modules.setdefault(ALIAS, _sys.modules[__name__])
+    for _sub in ("_lib", "ops", "synth"):
+        _sys.modules.setdefault(f"{ALIAS}.{_sub}", _sys.modules[f"{__name__}.{_sub}"])
+
+__all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "install", "uninstall",
+           "KdaError", "KdaLibraryError", "load_library"]
+
+
+def load_library():
+    """Load ``libkda_b200.so`` now (raises :class:`KdaLibraryError` if absent)."""
+    return _lib.load()
+
+
+_saved = []
+
+
+def install(kda_module=None, package=None):
+    """Point the reference's KDA kernels at this package.
+
+    Replaces ``kda_chunkwise`` / ``kda_recurrent`` in ``kimi_linear.kda`` (or the
+    module object ``kda_module``) and in the ``kimi_linear`` package namespace,
+    which re-exports them by value (``kimi_linear/__init__.py:9``).  Loads the
+    CUDA library first, so a missing build fails here rather than mid-model.
+    Returns the list of patched ``(module, name)`` pairs; :func:`uninstall`
+    restores the originals.
+    """
+    import importlib
+
+    _lib.load()
+    if kda_module is None:
+        kda_module = importlib.import_module("kimi_linear.kda")
+    if package is None:
+        pkg_name = kda_module.__name__.rpartition(".")[0]
+        package = _sys.modules.get(pkg_name) if pkg_name else None
+    patched = []
+    for mod in (kda_module, package):
+        if mod is None:
+            continue
+        for name, fn in (("kda_chunkwise", kda_chunkwise), ("kda_recurrent", kda_recurrent)):
+            if hasattr(mod, name) and getattr(mod, name) is not fn:
+                _saved.append((mod, name, getattr(mod, name)))
+                setattr(mod, name, fn)
+                patched.append((mod.__name__, name))
+    return patched
+
+
+def uninstall():
+    """Undo every :func:`install` (most recent first)."""
+    while _saved:
+        mod, name, fn = _saved.pop()
+        setattr(mod, name, fn)

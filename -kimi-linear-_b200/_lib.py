@@ -1,0 +1,133 @@
+"""ctypes binding of ``libkda_b200.so`` (the C ABI in ``include/kda_b200.h``).
+
+The library is loaded lazily on first use.  If it is missing or does not load,
+:class:`KdaLibraryError` is raised: the KDA entry points have no CPU or
+pure-PyTorch fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkda_b200.so")
+
+ABI_VERSION = 1
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+
+# kda_status_t
+KDA_OK = 0
+KDA_ERR_NULL_POINTER = 1
+KDA_ERR_SHAPE = 2
+KDA_ERR_DTYPE = 3
+KDA_ERR_STRIDE = 4
+KDA_ERR_ALIGNMENT = 5
+KDA_ERR_ARCH = 6
+KDA_ERR_LAUNCH = 7
+KDA_ERR_CHUNK = 8
+KDA_ERR_WORKSPACE = 9
+KDA_ERR_CUDA = 10
+
+# every symbol include/kda_b200.h declares
+EXPORTED = (
+    "kda_chunkwise_fwd",
+    "kda_recurrent_fwd",
+    "kda_chunkwise_workspace_bytes",
+    "kda_chunkwise_path",
+    "kda_status_string",
+    "kda_device_supported",
+    "kda_args_size",
+    "kda_abi_version",
+)
+
+_I64x4 = ctypes.c_int64 * 4
+_I64x3 = ctypes.c_int64 * 3
+
+
+class KdaArgs(ctypes.Structure):
+    """Mirror of ``struct KdaArgs`` (field order and types must match)."""
+
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("H", ctypes.c_int32),
+        ("K", ctypes.c_int32), ("V", ctypes.c_int32),
+        ("chunk_size", ctypes.c_int32),
+        ("io_dtype", ctypes.c_int32),
+        ("state_in_dtype", ctypes.c_int32),
+        ("state_out_dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q", ctypes.c_void_p), ("q_stride", _I64x4),
+        ("k", ctypes.c_void_p), ("k_stride", _I64x4),
+        ("v", ctypes.c_void_p), ("v_stride", _I64x4),
+        ("g", ctypes.c_void_p), ("g_stride", _I64x4),
+        ("beta", ctypes.c_void_p), ("beta_stride", _I64x3),
+        ("state_in", ctypes.c_void_p), ("state_in_stride", _I64x4),
+        ("o", ctypes.c_void_p), ("o_stride", _I64x4),
+        ("state_out", ctypes.c_void_p), ("state_out_stride", _I64x4),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class KdaLibraryError(RuntimeError):
+    """The CUDA library is missing or unusable (there is no fallback path)."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib):
+    P = ctypes.POINTER(KdaArgs)
+    lib.kda_chunkwise_fwd.argtypes = [P, ctypes.c_void_p]
+    lib.kda_chunkwise_fwd.restype = ctypes.c_int
+    lib.kda_recurrent_fwd.argtypes = [P, ctypes.c_void_p]
+    lib.kda_recurrent_fwd.restype = ctypes.c_int
+    lib.kda_chunkwise_workspace_bytes.argtypes = [P]
+    lib.kda_chunkwise_workspace_bytes.restype = ctypes.c_size_t
+    lib.kda_chunkwise_path.argtypes = [P]
+    lib.kda_chunkwise_path.restype = ctypes.c_int
+    lib.kda_status_string.argtypes = [ctypes.c_int]
+    lib.kda_status_string.restype = ctypes.c_char_p
+    lib.kda_device_supported.argtypes = [ctypes.c_int]
+    lib.kda_device_supported.restype = ctypes.c_int
+    lib.kda_args_size.argtypes = []
+    lib.kda_args_size.restype = ctypes.c_size_t
+    lib.kda_abi_version.argtypes = []
+    lib.kda_abi_version.restype = ctypes.c_int
+
+
+def load(path: str | None = None):
+    """Load (once) and return the ctypes library handle."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise KdaLibraryError(
+                f"{p} is missing: build it with __graft_entry__.build() or "
+                f"'python -m kimi_linear_b200.build' (nvcc, sm_100a)")
+        try:
+            lib = ctypes.CDLL(p)
+        except OSError as exc:  # pragma: no cover - depends on the host
+            raise KdaLibraryError(f"cannot load {p}: {exc}") from exc
+        missing = [s for s in EXPORTED if not hasattr(lib, s)]
+        if missing:
+            raise KdaLibraryError(f"{p} lacks symbols {missing}")
+        _declare(lib)
+        if lib.kda_abi_version() != ABI_VERSION:
+            raise KdaLibraryError(f"{p}: ABI version {lib.kda_abi_version()} != {ABI_VERSION}")
+        if lib.kda_args_size() != ctypes.sizeof(KdaArgs):
+            raise KdaLibraryError(
+                f"{p}: sizeof(KdaArgs) {lib.kda_args_size()} != ctypes {ctypes.sizeof(KdaArgs)}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(code: int) -> str:
+    return load().kda_status_string(int(code)).decode()

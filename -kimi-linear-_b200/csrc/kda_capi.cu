@@ -1,0 +1,202 @@
+// kda_capi.cu -- extern "C" entry points declared in include/kda_b200.h.
+//
+// Validates a KdaArgs block (shapes, dtypes, strides, alignment, device
+// architecture), converts it to the kernels' parameter block and launches on
+// the caller's stream.  Nothing here synchronises, allocates or reads device
+// memory, so both entry points can be captured in a CUDA graph.
+#include <cstring>
+#include <mutex>
+
+#include "kda_internal.cuh"
+
+namespace kda {
+
+size_t chunk_simt_smem_bytes(int K);
+// tensor-core path (kda_chunk_tc.cu)
+bool chunk_tc_supported(const ChunkParams& p);
+size_t chunk_tc_workspace_bytes(const ChunkParams& p);
+cudaError_t launch_chunk_tc(const ChunkParams& p, void* workspace, cudaStream_t s);
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+int g_arch_ok[kMaxDevices];   // 0 = unknown, 1 = sm_100, -1 = other
+std::mutex g_arch_mu;
+
+int elt_size(int dt) { return dt == KDA_DTYPE_F32 ? 4 : 2; }
+bool dtype_ok(int dt) { return dt == KDA_DTYPE_F32 || dt == KDA_DTYPE_F16 || dt == KDA_DTYPE_BF16; }
+
+// 1 when the current device is compute capability 10.0 (B200 family).
+int check_arch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KDA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return KDA_ERR_ARCH;
+  int known = __atomic_load_n(&g_arch_ok[dev], __ATOMIC_ACQUIRE);
+  if (known == 0) {
+    std::lock_guard<std::mutex> lk(g_arch_mu);
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return KDA_ERR_CUDA;
+    known = (major == 10 && minor == 0) ? 1 : -1;
+    __atomic_store_n(&g_arch_ok[dev], known, __ATOMIC_RELEASE);
+  }
+  return known == 1 ? KDA_OK : KDA_ERR_ARCH;
+}
+
+// 4 consecutive innermost elements at any row start are 4-element aligned.
+bool vec4_ok(const void* ptr, const int64_t* stride, int ndim_outer, int dt) {
+  const uintptr_t align = (uintptr_t)(4 * elt_size(dt));
+  if ((reinterpret_cast<uintptr_t>(ptr) % align) != 0) return false;
+  for (int d = 0; d < ndim_outer; ++d)
+    if (stride[d] % 4 != 0) return false;
+  return true;
+}
+
+int validate(const KdaArgs* a, bool chunkwise) {
+  if (a == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
+  if (a->B < 0 || a->T < 0 || a->H < 0 || a->K < 1 || a->V < 1) return KDA_ERR_SHAPE;
+  if (a->K > kRecMaxK || a->K > kSimtMaxK) return KDA_ERR_SHAPE;
+  if (a->B > 65535 || a->H > 65535) return KDA_ERR_SHAPE;
+  if (!dtype_ok(a->io_dtype) || !dtype_ok(a->state_out_dtype)) return KDA_ERR_DTYPE;
+  if (a->state_in != nullptr && !dtype_ok(a->state_in_dtype)) return KDA_ERR_DTYPE;
+  if (chunkwise) {
+    if (a->chunk_size < 1) return KDA_ERR_CHUNK;
+    if (a->T % a->chunk_size != 0) return KDA_ERR_CHUNK;
+  }
+  if (a->B == 0 || a->H == 0) return KDA_OK;   // nothing to compute
+  if (a->state_out == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->T > 0 &&
+      (a->q == nullptr || a->k == nullptr || a->v == nullptr || a->g == nullptr ||
+       a->beta == nullptr || a->o == nullptr))
+    return KDA_ERR_NULL_POINTER;
+  if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 ||
+      a->g_stride[3] != 1 || a->o_stride[3] != 1 || a->state_out_stride[3] != 1)
+    return KDA_ERR_STRIDE;
+  if (a->state_in != nullptr && a->state_in_stride[3] != 1) return KDA_ERR_STRIDE;
+  // natural alignment of every element pointer
+  const uintptr_t e = (uintptr_t)elt_size(a->io_dtype);
+  if ((reinterpret_cast<uintptr_t>(a->q) % e) || (reinterpret_cast<uintptr_t>(a->k) % e) ||
+      (reinterpret_cast<uintptr_t>(a->v) % e) || (reinterpret_cast<uintptr_t>(a->o) % e) ||
+      (reinterpret_cast<uintptr_t>(a->g) % 4) || (reinterpret_cast<uintptr_t>(a->beta) % 4))
+    return KDA_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(a->state_out) % (uintptr_t)elt_size(a->state_out_dtype))
+    return KDA_ERR_ALIGNMENT;
+  if (a->state_in != nullptr &&
+      reinterpret_cast<uintptr_t>(a->state_in) % (uintptr_t)elt_size(a->state_in_dtype))
+    return KDA_ERR_ALIGNMENT;
+  return KDA_OK;
+}
+
+RecParams to_params(const KdaArgs* a) {
+  RecParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.B = a->B; p.T = a->T; p.H = a->H; p.K = a->K; p.V = a->V;
+  p.io_dtype = a->io_dtype;
+  p.state_in_dtype = a->state_in != nullptr ? a->state_in_dtype : KDA_DTYPE_F32;
+  p.state_out_dtype = a->state_out_dtype;
+  p.scale = a->scale;
+  p.q = a->q; p.k = a->k; p.v = a->v; p.g = a->g; p.beta = a->beta;
+  p.state_in = a->state_in; p.o = a->o; p.state_out = a->state_out;
+  for (int d = 0; d < 4; ++d) {
+    p.q_s[d] = a->q_stride[d]; p.k_s[d] = a->k_stride[d]; p.v_s[d] = a->v_stride[d];
+    p.g_s[d] = a->g_stride[d]; p.o_s[d] = a->o_stride[d];
+    p.si_s[d] = a->state_in_stride[d]; p.so_s[d] = a->state_out_stride[d];
+  }
+  for (int d = 0; d < 3; ++d) p.b_s[d] = a->beta_stride[d];
+  p.state_vec = a->state_in != nullptr && vec4_ok(a->state_in, a->state_in_stride, 3,
+                                                  a->state_in_dtype);
+  p.state_out_vec = vec4_ok(a->state_out, a->state_out_stride, 3, a->state_out_dtype);
+  p.o_vec = vec4_ok(a->o, a->o_stride, 3, a->io_dtype);
+  return p;
+}
+
+int launch_status(cudaError_t e) {
+  if (e == cudaSuccess) return KDA_OK;
+  return (e == cudaErrorInvalidConfiguration || e == cudaErrorLaunchFailure ||
+          e == cudaErrorInvalidValue || e == cudaErrorLaunchOutOfResources)
+             ? KDA_ERR_LAUNCH
+             : KDA_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace kda
+
+using namespace kda;
+
+extern "C" {
+
+int kda_recurrent_fwd(const KdaArgs* args, void* stream) {
+  int st = validate(args, /*chunkwise=*/false);
+  if (st != KDA_OK) return st;
+  if (args->B == 0 || args->H == 0) return KDA_OK;
+  st = check_arch();
+  if (st != KDA_OK) return st;
+  const RecParams p = to_params(args);
+  return launch_status(launch_recurrent(p, static_cast<cudaStream_t>(stream)));
+}
+
+int kda_chunkwise_path(const KdaArgs* args) {
+  int st = validate(args, /*chunkwise=*/true);
+  if (st != KDA_OK) return -st;
+  const RecParams p = to_params(args);
+  return chunk_tc_supported(p) ? 1 : 0;
+}
+
+size_t kda_chunkwise_workspace_bytes(const KdaArgs* args) {
+  if (validate(args, /*chunkwise=*/true) != KDA_OK) return 0;
+  const RecParams p = to_params(args);
+  return chunk_tc_supported(p) ? chunk_tc_workspace_bytes(p) : 0;
+}
+
+int kda_chunkwise_fwd(const KdaArgs* args, void* stream) {
+  int st = validate(args, /*chunkwise=*/true);
+  if (st != KDA_OK) return st;
+  if (args->B == 0 || args->H == 0) return KDA_OK;
+  st = check_arch();
+  if (st != KDA_OK) return st;
+  const RecParams p = to_params(args);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (chunk_tc_supported(p)) {
+    const size_t need = chunk_tc_workspace_bytes(p);
+    if (need > 0 && (args->workspace == nullptr || args->workspace_bytes < need))
+      return KDA_ERR_WORKSPACE;
+    if (need > 0 && (reinterpret_cast<uintptr_t>(args->workspace) % 256) != 0)
+      return KDA_ERR_ALIGNMENT;
+    return launch_status(launch_chunk_tc(p, args->workspace, s));
+  }
+  return launch_status(launch_chunk_simt(p, s));
+}
+
+const char* kda_status_string(int status) {
+  switch (status) {
+    case KDA_OK: return "ok";
+    case KDA_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case KDA_ERR_SHAPE: return "unsupported shape (need K <= 256, B and H <= 65535) or ABI mismatch";
+    case KDA_ERR_DTYPE: return "unsupported dtype (f32, f16 or bf16)";
+    case KDA_ERR_STRIDE: return "innermost stride must be 1";
+    case KDA_ERR_ALIGNMENT: return "pointer is not aligned to its element size";
+    case KDA_ERR_ARCH: return "device is not an sm_100 (B200) GPU";
+    case KDA_ERR_LAUNCH: return "kernel launch failed";
+    case KDA_ERR_CHUNK: return "T is not a multiple of chunk_size";
+    case KDA_ERR_WORKSPACE: return "workspace missing or too small";
+    case KDA_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int kda_device_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess)
+    return -1;
+  if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+    return -1;
+  return (major == 10 && minor == 0) ? 1 : 0;
+}
+
+size_t kda_args_size(void) { return sizeof(KdaArgs); }
+
+int kda_abi_version(void) { return KDA_B200_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,33 @@
+// kda_internal.cuh -- parameter blocks shared by the C-ABI layer and kernels.
+#pragma once
+
+#include "kda_common.cuh"
+
+namespace kda {
+
+constexpr int kRecMaxK = 256;    // recurrent kernel: K <= 256, any V
+constexpr int kSimtMaxK = 256;   // SIMT chunkwise kernel: K <= 256, any V
+
+// Device-side view of KdaArgs (strides in elements, innermost stride == 1).
+struct RecParams {
+  int B, T, H, K, V;
+  int io_dtype, state_in_dtype, state_out_dtype;
+  float scale;
+  const void* q; int64_t q_s[4];
+  const void* k; int64_t k_s[4];
+  const void* v; int64_t v_s[4];
+  const float* g; int64_t g_s[4];
+  const float* beta; int64_t b_s[3];
+  const void* state_in; int64_t si_s[4];
+  void* o; int64_t o_s[4];
+  void* state_out; int64_t so_s[4];
+  // 16-byte vector access is legal for 4 consecutive columns
+  bool state_vec, state_out_vec, o_vec;
+};
+
+using ChunkParams = RecParams;
+
+cudaError_t launch_recurrent(const RecParams& p, cudaStream_t s);
+cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t s);
+
+}  // namespace kda

@@ -1,0 +1,399 @@
+"""KDA core benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kda|reference]
+
+Workload: chunkwise KDA prefill, B=1, T=4096, H=16,
+K=V=128, reference chunk_size 64, fp16 q/k/v, fp32 g/beta, zero S0, fp32
+state out.  A step is one ``kda_chunkwise`` call over that batch.  Under
+torchrun each rank runs its own batch (weak scaling; the (b, h) recurrences
+are independent, so there is no collective on the data path).
+
+Reported, all on the device with CUDA events on the launching stream:
+
+* ``value``     prefill tokens/s of the whole job (sum over ranks; time is the
+                max over ranks), L2 flushed before every step;
+* ``roofline``  the chunkwise kernel against measured HBM bandwidth (the
+                workload is HBM-bound: ~116 FLOP/B < ~255 FLOP/B ridge);
+* ``e2e``       the same metric through the public API from pinned host
+                buffers: H2D of q/k/v/g/beta and D2H of o and S inside the
+                timed region;
+* ``decode``    BASELINE configs[2]: B=64 recurrent single-token steps on a
+                fp32 [64,16,128,128] state, against HBM bandwidth;
+* ``cpu_baseline`` the CPU oracle (oracle/kda_oracle.py, a numpy port of the
+                reference) on a bounded sample, rank 0 at N=1.
+
+``--impl reference`` times that CPU port alone, with all host cores, on the
+same workload and metric (the reference is pure PyTorch with no GPU kernels of
+its own; rank 0 only under torchrun).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "KDA prefill & decode tokens/s per GPU (H16,d128); % of TC/HBM roofline"
+CFG1 = dict(B=1, T=4096, H=16, K=128, V=128, C=64)
+CFG2 = dict(B=64, H=16, K=128, V=128)
+FLOP_PER_TOKEN_HEAD = 180224          # 2*[C(3K+2V) + 3KV] at C=64, K=V=128
+L2_FLUSH_BYTES = 512 << 20            # 4x the 126 MB L2
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def _traffic(kernel, workload):
+    """dram read+write bytes per launch from the committed ncu summary, or None."""
+    path = os.path.join(REPO, "profiles", "ncu_traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 3 and parts[0] == kernel and parts[1] == workload:
+                return float(parts[2])
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------- #
+# clocks sampled during the timed region
+# --------------------------------------------------------------------------- #
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.strip()]
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- #
+# CPU port (oracle) timing -- used by the cpu_baseline leg and --impl reference
+# --------------------------------------------------------------------------- #
+def _oracle_worker(args):
+    """One head of the config-1 workload on one core (spawned process)."""
+    T, K, V, C, seed, head = args
+    import numpy as np
+    from oracle import kda_oracle as O
+    rng = np.random.default_rng(seed * 1000 + head)
+
+    def unit(shape):
+        x = rng.standard_normal(shape).astype(np.float32)
+        return x / np.sqrt((x * x).sum(-1, keepdims=True))
+    # fp16-valued q/k/v carried in fp32: the port then runs the reference's
+    # fp32-transient arithmetic (kda.py:116), 13x faster in numpy than
+    # emulating fp16 transients and 2x faster than the reference's own torch
+    # fp16 run on the same CPU -- a conservative (fast) baseline
+    q = unit((1, T, 1, K)).astype(np.float16).astype(np.float32)
+    k = unit((1, T, 1, K)).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((1, T, 1, V)).astype(np.float16).astype(np.float32)
+    a_log = np.log(rng.uniform(1, 16, (1, K))).astype(np.float32)
+    x = rng.standard_normal((1, T, 1, K)).astype(np.float32)
+    dt = rng.uniform(1e-3, 0.1, (1, K)).astype(np.float32)
+    dt_bias = np.log(np.expm1(dt))
+    g = (-np.exp(a_log) * np.logaddexp(0, x + dt_bias)).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((1, T, 1))))).astype(np.float32)
+    t0 = time.perf_counter()
+    O.kda_chunkwise(q, k, v, g, beta, chunk_size=C, state_dtype="f32")
+    return time.perf_counter() - t0
+
+
+def cpu_port_throughput(t_sample, heads, steps=1, warmup=0):
+    """Config-1-equivalent tokens/s of the numpy port on ``heads`` host cores.
+
+    A step runs ``heads`` independent heads of length ``t_sample`` in a spawn
+    pool (one head per process); a config-1 token is 16 heads, so a step
+    covers ``t_sample * heads / 16`` tokens.
+    """
+    import multiprocessing as mp
+    env_keys = ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")
+    old = {k: os.environ.get(k) for k in env_keys}
+    for k in env_keys:
+        os.environ[k] = "1"
+    try:
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(heads) as pool:
+            times = []
+            for s in range(warmup + steps):
+                job = [(t_sample, CFG1["K"], CFG1["V"], CFG1["C"], s, h) for h in range(heads)]
+                per_head = pool.map(_oracle_worker, job)
+                if s >= warmup:
+                    times.append(max(per_head))
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    wall = sum(times) / len(times)
+    tokens = t_sample * heads / CFG1["H"]
+    return tokens / wall, wall
+
+
+# --------------------------------------------------------------------------- #
+# GPU legs
+# --------------------------------------------------------------------------- #
+def _events_time(torch, fn, steps, warmup, flush):
+    """Mean device ms of ``fn`` over ``steps`` runs, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+
+
+def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world):
+    x = kb.synth.make_config(1, seed=0, device=dev)
+    q, k, v, g, beta = (x[n] for n in ("q", "k", "v", "g", "beta"))
+    f32 = torch.float32
+
+    def step():
+        return kb.kda_chunkwise(q, k, v, g, beta, chunk_size=CFG1["C"], state_dtype=f32)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with ClockSampler(dev.index) as clk:
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    ms_step = total.item() / steps
+
+    # end to end through the public API from pinned host memory
+    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("g", g),
+                                                  ("beta", beta))}
+    o_h = torch.empty((CFG1["B"], CFG1["T"], CFG1["H"], CFG1["V"]), dtype=v.dtype).pin_memory()
+    S_h = torch.empty((CFG1["B"], CFG1["H"], CFG1["K"], CFG1["V"]), dtype=f32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = o_h.numel() * o_h.element_size() + S_h.numel() * S_h.element_size()
+
+    def e2e_step():
+        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+        o, S = kb.kda_chunkwise(d["q"], d["k"], d["v"], d["g"], d["beta"],
+                                chunk_size=CFG1["C"], state_dtype=f32)
+        o_h.copy_(o, non_blocking=True)
+        S_h.copy_(S, non_blocking=True)
+
+    e2e_steps = max(5, steps // 4)
+    e2e_ms = _events_time(torch, e2e_step, e2e_steps, 2, flush)
+    e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    path = kb.chunkwise_path(q, k, v, g, beta, chunk_size=CFG1["C"], state_dtype=f32)
+    return ms_step, e2e_t.item(), h2d, d2h, clk.summary(), path
+
+
+def bench_decode(torch, kb, dev, steps, warmup, flush):
+    """Config 2: single-token recurrent steps on a fp32 [64,16,128,128] state."""
+    B, H, K, V = CFG2["B"], CFG2["H"], CFG2["K"], CFG2["V"]
+    gen = torch.Generator(device=dev).manual_seed(2)
+    x = kb.synth.make_inputs(B, steps + warmup, H, K, V, dtype=torch.float16, seed=2,
+                             s0_std=0.02, device=dev, generator=gen)
+    state = [x["S0"]]
+    t = [0]
+
+    def step():
+        i = t[0] % (steps + warmup)
+        t[0] += 1
+        o, S = kb.kda_recurrent(*(x[n][:, i:i + 1] for n in ("q", "k", "v", "g", "beta")),
+                                state=state[0], state_dtype=torch.float32)
+        state[0] = S
+        return o
+
+    ms = _events_time(torch, step, steps, warmup, flush)
+    return ms
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("kda", "reference"), default="kda")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if a.impl == "reference":
+        if rank != 0:
+            return
+        heads = max(1, min(os.cpu_count() or 1, 16))
+        t_sample = 1024
+        val, wall = cpu_port_throughput(t_sample, heads, steps=a.steps, warmup=a.warmup)
+        line = {
+            "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": wall * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "kda_chunkwise prefill, BASELINE configs[1]", **CFG1,
+                       "sample": f"{heads} of 16 heads x {t_sample} tokens per step"},
+            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": heads, "kind": "port",
+                             "sample": f"{heads} heads x {t_sample} tokens of configs[1] per "
+                                       f"step, numpy port of kda.py:58-185, fp32 transients "
+                                       f"on fp16-valued inputs"},
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    kb = importlib.import_module("-kimi-linear-_b200")
+    kb.load_library()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as td
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                              device_id=dev)
+        dist = td
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    ms_step, e2e_ms, h2d, d2h, clocks, path = bench_prefill(
+        torch, kb, dev, a.steps, a.warmup, flush, dist, world)
+    dec_ms = bench_decode(torch, kb, dev, a.decode_steps, a.warmup, flush)
+    dec_t = torch.tensor([dec_ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(dec_t, op=dist.ReduceOp.MAX)
+    dec_ms = dec_t.item()
+
+    hbm, tc, peak_kind = _peaks()
+    tokens = CFG1["B"] * CFG1["T"]
+    th = tokens * CFG1["H"]
+    pre_bytes = th * (2 * CFG1["K"] * 2 + CFG1["V"] * 2 + CFG1["K"] * 4 + 4 + CFG1["V"] * 2) \
+        + CFG1["B"] * CFG1["H"] * CFG1["K"] * CFG1["V"] * 4
+    pre_flop = th * FLOP_PER_TOKEN_HEAD
+    dec_bytes = CFG2["B"] * CFG2["H"] * (2 * CFG2["K"] * CFG2["V"] * 4
+                                         + 2 * CFG2["K"] * 2 + CFG2["V"] * 2 + CFG2["K"] * 4
+                                         + 4 + CFG2["V"] * 2)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        heads = max(1, min(os.cpu_count() or 1, 16))
+        t_sample = 4096
+        val, wall = cpu_port_throughput(t_sample, heads, steps=2)
+        cpu = {"value": val, "unit": "tokens/s", "cores": heads, "kind": "port",
+               "sample": f"{heads} heads x {t_sample} tokens of configs[1] "
+                         f"({wall:.2f} s per step), numpy port of kda.py:58-185, fp32 "
+                         f"transients on fp16-valued inputs"}
+
+    if rank == 0:
+        ach = pre_bytes / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": world * tokens / (ms_step * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "kda_chunkwise prefill, BASELINE configs[1] per GPU",
+                       **CFG1, "state": "fp32", "parallelism": f"dp{world} over (b,h)",
+                       "kernel": path,
+                       "l2": "flushed before every step (512 MiB write)"},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "peak_kind": peak_kind,
+                         "traffic": _traffic("kda_chunkwise", "cfg1"),
+                         "algorithmic_bytes": pre_bytes,
+                         "tensor_frac": pre_flop / (ms_step * 1e-3) / (tc * 1e12)},
+            "e2e": {"value": world * tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "decode": {"workload": "kda_recurrent single-token step, BASELINE configs[2]",
+                       "value": world * CFG2["B"] / (dec_ms * 1e-3), "unit": "tokens/s",
+                       "ms_per_step": dec_ms, "steps": a.decode_steps,
+                       "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms * 1e-3) / 1e9,
+                                    "peak": hbm, "unit": "GB/s",
+                                    "frac": dec_bytes / (dec_ms * 1e-3) / 1e9 / hbm,
+                                    "traffic": _traffic("kda_recurrent", "cfg2"),
+                                    "algorithmic_bytes": dec_bytes}},
+            "gpu_launches": a.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

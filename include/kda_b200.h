@@ -1,0 +1,130 @@
+/*
+ * kda_b200.h -- C ABI of the B200 (sm_100a) Kimi Delta Attention core.
+ *
+ * Drop-in boundary for the two kernels of Lazy-Hakimi/-kimi-linear-:
+ *
+ *   kda_chunkwise_fwd  replaces kimi_linear/kda.py:58-185 (kda_chunkwise)
+ *   kda_recurrent_fwd  replaces kimi_linear/kda.py:188-219 (kda_recurrent)
+ *
+ * Plain pointers, sizes and element strides only.  The Python host layer
+ * (-kimi-linear-_b200/ops.py) keeps the reference's Python signatures and
+ * calls these entry points through ctypes; any other FFI can bind them the
+ * same way.
+ *
+ * Tensor conventions (identical to the reference):
+ *   q, k, g : [B, T, H, K]     v, o : [B, T, H, V]     beta : [B, T, H]
+ *   state   : [B, H, K, V]
+ * Strides are in ELEMENTS; the innermost (last) stride of every tensor must
+ * be 1.  g and beta are fp32 (the reference promotes them with .float(),
+ * kda.py:119-120,202-203).  q is multiplied by `scale` inside the kernel (the
+ * reference uses K^-0.5, kda.py:132,199).  Inputs are never written.
+ *
+ * Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
+ * default stream), performs no host<->device synchronisation, no allocation
+ * and no host read of device data, so it can be captured in a CUDA graph.
+ */
+#ifndef KDA_B200_H
+#define KDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_B200_ABI_VERSION 1
+
+/* Element types. */
+typedef enum {
+  KDA_DTYPE_F32 = 0,
+  KDA_DTYPE_F16 = 1,
+  KDA_DTYPE_BF16 = 2
+} kda_dtype_t;
+
+/* Status codes: 0 = success; the Python layer maps the rest to exceptions. */
+typedef enum {
+  KDA_OK = 0,
+  KDA_ERR_NULL_POINTER = 1, /* a required pointer is NULL                    */
+  KDA_ERR_SHAPE = 2,        /* a size is out of the supported range          */
+  KDA_ERR_DTYPE = 3,        /* unsupported dtype combination                 */
+  KDA_ERR_STRIDE = 4,       /* innermost stride != 1                          */
+  KDA_ERR_ALIGNMENT = 5,    /* pointer / stride alignment not met             */
+  KDA_ERR_ARCH = 6,         /* device is not sm_100 (B200 family)             */
+  KDA_ERR_LAUNCH = 7,       /* kernel launch failed (cudaGetLastError)        */
+  KDA_ERR_CHUNK = 8,        /* T is not a multiple of chunk_size (kda.py:124) */
+  KDA_ERR_WORKSPACE = 9,    /* workspace missing or too small                 */
+  KDA_ERR_CUDA = 10         /* another CUDA runtime error                     */
+} kda_status_t;
+
+/* Arguments shared by both entry points. */
+typedef struct KdaArgs {
+  int32_t abi_version;      /* must be KDA_B200_ABI_VERSION */
+  int32_t B, T, H, K, V;
+  int32_t chunk_size;       /* reference chunk_size; chunkwise only */
+  int32_t io_dtype;         /* dtype of q, k, v and o (kda_dtype_t) */
+  int32_t state_in_dtype;   /* dtype of state_in (ignored when NULL) */
+  int32_t state_out_dtype;  /* dtype of state_out */
+  float scale;              /* multiplier applied to q (K^-0.5 in the reference) */
+  const void* q;     int64_t q_stride[4];
+  const void* k;     int64_t k_stride[4];
+  const void* v;     int64_t v_stride[4];
+  const float* g;    int64_t g_stride[4];
+  const float* beta; int64_t beta_stride[3];
+  const void* state_in;  int64_t state_in_stride[4];  /* NULL = zero state */
+  void* o;           int64_t o_stride[4];
+  void* state_out;   int64_t state_out_stride[4];
+  void* workspace;          /* device scratch, >= kda_chunkwise_workspace_bytes() */
+  size_t workspace_bytes;
+} KdaArgs;
+
+/*
+ * Chunkwise KDA forward (paper Eq. 6-9).
+ * Reference: kimi_linear/kda.py:58-185, kda_chunkwise(q, k, v, g, beta,
+ * initial_state, chunk_size, tile_size, state_dtype) -> (o, S).
+ * state_in  = initial_state (kda.py:134-137); state_out = returned S
+ * (kda.py:185).  Returns KDA_ERR_CHUNK when T % chunk_size != 0, where the
+ * reference's reshape fails (kda.py:124).
+ */
+int kda_chunkwise_fwd(const KdaArgs* args, void* stream);
+
+/*
+ * Recurrent KDA forward (paper Eq. 1), any T >= 1.
+ * Reference: kimi_linear/kda.py:188-219, kda_recurrent(q, k, v, g, beta,
+ * state, state_dtype) -> (o, S).  fp16 outputs are clamped to +-60000
+ * (kda.py:217-218, FP16_MAX_SAFE of kimi_linear/fp16.py:97).
+ */
+int kda_recurrent_fwd(const KdaArgs* args, void* stream);
+
+/*
+ * Device scratch bytes kda_chunkwise_fwd needs for `args` (0 = none).
+ * No reference counterpart: the reference allocates its transients inside
+ * torch (kda.py:131-138,148-149).
+ */
+size_t kda_chunkwise_workspace_bytes(const KdaArgs* args);
+
+/*
+ * Which implementation kda_chunkwise_fwd selects for `args`:
+ * 0 = CUDA-core (SIMT) kernel, 1 = tcgen05 tensor-core kernel, <0 = status
+ * error.  No reference counterpart (diagnostic).
+ */
+int kda_chunkwise_path(const KdaArgs* args);
+
+/* Human-readable text for a status code.  No reference counterpart. */
+const char* kda_status_string(int status);
+
+/* 1 when `device` is an sm_100 GPU these kernels run on, 0 otherwise,
+ * <0 on a CUDA error.  No reference counterpart. */
+int kda_device_supported(int device);
+
+/* sizeof(KdaArgs) as compiled, for FFI layout checks. */
+size_t kda_args_size(void);
+
+/* KDA_B200_ABI_VERSION as compiled. */
+int kda_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_B200_H */

@@ -1,0 +1,116 @@
+"""Host-side behaviour of the reference-signature shim (no GPU needed):
+argument checking, the forward-only guard, the absence of any CPU path, and
+``install()`` patching the reference's module globals."""
+
+from __future__ import annotations
+
+import os
+import sys
+import types
+
+import pytest
+import torch
+
+from conftest import pkg
+
+
+def _inputs(T=64, dtype=torch.float32):
+    s = pkg().synth
+    return s.make_inputs(1, T, 2, 32, 32, dtype=dtype, seed=0)
+
+
+def test_cpu_tensors_raise_no_fallback():
+    x = _inputs()
+    kb = pkg()
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=64)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        kb.kda_recurrent(x["q"], x["k"], x["v"], x["g"], x["beta"])
+
+
+def test_ragged_t_raises_like_reference():
+    x = _inputs(T=40)
+    with pytest.raises(RuntimeError, match="multiple of chunk_size"):
+        pkg().kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=64)
+    with pytest.raises(ZeroDivisionError):
+        pkg().kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=0)
+
+
+def test_forward_only_guard():
+    x = _inputs()
+    q = x["q"].clone().requires_grad_(True)
+    with pytest.raises(RuntimeError):
+        pkg().kda_recurrent(q, x["k"], x["v"], x["g"], x["beta"])
+
+
+def test_package_alias_registered():
+    import importlib
+    kb = pkg()
+    assert importlib.import_module("kimi_linear_b200") is kb
+    assert sys.modules["kimi_linear_b200.ops"] is kb.ops
+
+
+def _fake_reference():
+    """Module objects shaped like kimi_linear and kimi_linear.kda."""
+    pkg_mod = types.ModuleType("fake_kimi_linear")
+    kda_mod = types.ModuleType("fake_kimi_linear.kda")
+
+    def ref_chunk(*a, **k):
+        return "reference-chunkwise"
+
+    def ref_rec(*a, **k):
+        return "reference-recurrent"
+
+    kda_mod.kda_chunkwise, kda_mod.kda_recurrent = ref_chunk, ref_rec
+    pkg_mod.kda_chunkwise, pkg_mod.kda_recurrent = ref_chunk, ref_rec
+    pkg_mod.kda = kda_mod
+    return pkg_mod, kda_mod, ref_chunk, ref_rec
+
+
+def test_install_patches_module_and_package_reexports():
+    kb = pkg()
+    pkg_mod, kda_mod, ref_chunk, ref_rec = _fake_reference()
+    patched = kb.install(kda_module=kda_mod, package=pkg_mod)
+    try:
+        assert kda_mod.kda_chunkwise is kb.kda_chunkwise
+        assert kda_mod.kda_recurrent is kb.kda_recurrent
+        assert pkg_mod.kda_chunkwise is kb.kda_chunkwise
+        assert pkg_mod.kda_recurrent is kb.kda_recurrent
+        assert len(patched) == 4
+    finally:
+        kb.uninstall()
+    assert kda_mod.kda_chunkwise is ref_chunk and pkg_mod.kda_recurrent is ref_rec
+
+
+REF = os.environ.get("KDA_REFERENCE_PATH", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "kimi_linear")),
+                    reason="reference checkout not present on this host")
+def test_reference_module_routes_through_patch():
+    """With the reference checkout importable, KimiDeltaAttention.forward
+    reaches the patched kernels (it resolves them at call time,
+    kda.py:503,519,526): on CPU tensors our entry point raises its
+    'needs CUDA tensors' error, which proves the routing."""
+    sys.path.insert(0, REF)
+    try:
+        import kimi_linear
+        from kimi_linear.configuration import KimiLinearConfig
+        from kimi_linear.kda import KimiDeltaAttention
+        kb = pkg()
+        cfg = KimiLinearConfig.from_json(os.path.join(REF, "configs", "kimi_linear_tiny_test.json"))
+        mod = KimiDeltaAttention(cfg)
+        x = torch.randn(1, 32, cfg.hidden_size)
+        kb.install()
+        try:
+            assert kimi_linear.kda_chunkwise is kb.kda_chunkwise
+            with torch.no_grad(), pytest.raises(RuntimeError, match="CUDA tensors"):
+                mod(x)
+            with torch.no_grad(), pytest.raises(RuntimeError, match="CUDA tensors"):
+                mod(x[:, :1], use_cache=True)
+        finally:
+            kb.uninstall()
+        with torch.no_grad():
+            assert mod(x).shape == x.shape   # the reference path again
+    finally:
+        sys.path.remove(REF)

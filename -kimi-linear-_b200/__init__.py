@@ -26,7 +26,7 @@ import sys as _sys
 
 from . import _lib, ops, synth
 from ._lib import KdaLibraryError
-from .ops import KdaError, chunkwise_path, kda_chunkwise, kda_recurrent
+from .ops import KdaError, chunkwise_impl, chunkwise_path, device_error, kda_chunkwise, kda_recurrent
 
 ALIAS = "kimi_linear_b200"
 if __name__ != ALIAS:
@@ -34,7 +34,8 @@ if __name__ != ALIAS:
     for _sub in ("_lib", "ops", "synth"):
         _sys.modules.setdefault(f"{ALIAS}.{_sub}", _sys.modules[f"{__name__}.{_sub}"])
 
-__all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "install", "uninstall",
+__all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "chunkwise_impl", "device_error",
+           "install", "uninstall",
            "KdaError", "KdaLibraryError", "load_library"]
 
 

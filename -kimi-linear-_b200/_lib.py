@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(HERE, "libkda_b200.so")
 ABI_VERSION = 1
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+FLAG_FORCE_SIMT = 1
 
 # kda_status_t
 KDA_OK = 0
@@ -39,6 +40,7 @@ EXPORTED = (
     "kda_chunkwise_path",
     "kda_status_string",
     "kda_device_supported",
+    "kda_device_error",
     "kda_args_size",
     "kda_abi_version",
 )
@@ -59,6 +61,7 @@ class KdaArgs(ctypes.Structure):
         ("state_in_dtype", ctypes.c_int32),
         ("state_out_dtype", ctypes.c_int32),
         ("scale", ctypes.c_float),
+        ("flags", ctypes.c_int32),
         ("q", ctypes.c_void_p), ("q_stride", _I64x4),
         ("k", ctypes.c_void_p), ("k_stride", _I64x4),
         ("v", ctypes.c_void_p), ("v_stride", _I64x4),
@@ -94,6 +97,8 @@ def _declare(lib):
     lib.kda_status_string.restype = ctypes.c_char_p
     lib.kda_device_supported.argtypes = [ctypes.c_int]
     lib.kda_device_supported.restype = ctypes.c_int
+    lib.kda_device_error.argtypes = [ctypes.c_int]
+    lib.kda_device_error.restype = ctypes.c_int
     lib.kda_args_size.argtypes = []
     lib.kda_args_size.restype = ctypes.c_size_t
     lib.kda_abi_version.argtypes = []

@@ -11,11 +11,6 @@
 
 namespace kda {
 
-size_t chunk_simt_smem_bytes(int K);
-// tensor-core path (kda_chunk_tc.cu)
-bool chunk_tc_supported(const ChunkParams& p);
-size_t chunk_tc_workspace_bytes(const ChunkParams& p);
-cudaError_t launch_chunk_tc(const ChunkParams& p, void* workspace, cudaStream_t s);
 
 namespace {
 
@@ -50,6 +45,14 @@ bool vec4_ok(const void* ptr, const int64_t* stride, int ndim_outer, int dt) {
   if ((reinterpret_cast<uintptr_t>(ptr) % align) != 0) return false;
   for (int d = 0; d < ndim_outer; ++d)
     if (stride[d] % 4 != 0) return false;
+  return true;
+}
+
+// 8 consecutive 16-bit innermost elements at any row start are 16-byte aligned.
+bool vec8_ok(const void* ptr, const int64_t* stride) {
+  if ((reinterpret_cast<uintptr_t>(ptr) % 16) != 0) return false;
+  for (int d = 0; d < 3; ++d)
+    if (stride[d] % 8 != 0) return false;
   return true;
 }
 
@@ -109,6 +112,9 @@ RecParams to_params(const KdaArgs* a) {
                                                   a->state_in_dtype);
   p.state_out_vec = vec4_ok(a->state_out, a->state_out_stride, 3, a->state_out_dtype);
   p.o_vec = vec4_ok(a->o, a->o_stride, 3, a->io_dtype);
+  p.v_vec16 = a->io_dtype != KDA_DTYPE_F32 && vec8_ok(a->v, a->v_stride);
+  p.o_vec16 = a->io_dtype != KDA_DTYPE_F32 && vec8_ok(a->o, a->o_stride);
+  p.force_simt = (a->flags & KDA_FLAG_FORCE_SIMT) != 0;
   return p;
 }
 
@@ -194,6 +200,8 @@ int kda_device_supported(int device) {
     return -1;
   return (major == 10 && minor == 0) ? 1 : 0;
 }
+
+int kda_device_error(int clear) { return read_device_error(clear != 0); }
 
 size_t kda_args_size(void) { return sizeof(KdaArgs); }
 

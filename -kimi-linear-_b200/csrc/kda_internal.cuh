@@ -23,11 +23,20 @@ struct RecParams {
   void* state_out; int64_t so_s[4];
   // 16-byte vector access is legal for 4 consecutive columns
   bool state_vec, state_out_vec, o_vec;
+  // 16-byte access is legal for 8 consecutive 16-bit v / o elements
+  bool v_vec16, o_vec16;
+  // run the CUDA-core chunkwise kernel even where the tensor-core one applies
+  bool force_simt;
 };
 
 using ChunkParams = RecParams;
 
 cudaError_t launch_recurrent(const RecParams& p, cudaStream_t s);
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t s);
+bool chunk_tc_supported(const ChunkParams& p);
+size_t chunk_tc_workspace_bytes(const ChunkParams& p);
+cudaError_t launch_chunk_tc(const ChunkParams& p, void* workspace, cudaStream_t s);
+// error word set by kernels whose bounded waits gave up (0 = none)
+int read_device_error(bool clear);
 
 }  // namespace kda

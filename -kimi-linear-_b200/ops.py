@@ -86,6 +86,7 @@ def _fill(args, q, k, v, g, beta, state_in, o, state_out, chunk_size):
     args.io_dtype = _DT[v.dtype]
     args.state_out_dtype = _DT[state_out.dtype]
     args.scale = float(K) ** -0.5
+    args.flags = 0
     args.q, args.q_stride = q.data_ptr(), _strides(q, 4)
     args.k, args.k_stride = k.data_ptr(), _strides(k, 4)
     args.v, args.v_stride = v.data_ptr(), _strides(v, 4)
@@ -151,6 +152,14 @@ def _call(fn_name, entry, args, dev):
 def kda_chunkwise(q, k, v, g, beta, initial_state=None, chunk_size=64, tile_size=0,
                   state_dtype=None):
     """Chunkwise KDA forward -- drop-in for ``kimi_linear/kda.py:58``."""
+    return chunkwise_impl(q, k, v, g, beta, initial_state, chunk_size, state_dtype)
+
+
+def chunkwise_impl(q, k, v, g, beta, initial_state=None, chunk_size=64, state_dtype=None,
+                   force_simt=False):
+    """``kda_chunkwise`` with an implementation switch: ``force_simt=True``
+    runs the CUDA-core kernel even where the tcgen05 kernel applies (both
+    are complete implementations; the switch exists to cross-check them)."""
     C = int(chunk_size)
     if C == 0:
         raise ZeroDivisionError("integer division or modulo by zero")  # T // C, kda.py:114
@@ -166,6 +175,8 @@ def kda_chunkwise(q, k, v, g, beta, initial_state=None, chunk_size=64, tile_size
     lib = _lib.load()
     args = _lib.KdaArgs()
     _fill(args, q, k, v, g, beta, s0, o, S, C)
+    if force_simt:
+        args.flags = _lib.FLAG_FORCE_SIMT
     need = lib.kda_chunkwise_workspace_bytes(ctypes.byref(args))
     if need:
         ws = torch.empty(int(need), dtype=torch.uint8, device=dev)
@@ -186,6 +197,11 @@ def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None):
     _fill(args, q, k, v, g, beta, s0, o, S, 1)
     _call("kda_recurrent", lib.kda_recurrent_fwd, args, dev)
     return o, S
+
+
+def device_error(clear=True):
+    """The kernels' device error word (0 = no bounded wait ever gave up)."""
+    return int(_lib.load().kda_device_error(1 if clear else 0))
 
 
 def chunkwise_path(q, k, v, g, beta, initial_state=None, chunk_size=64, state_dtype=None):

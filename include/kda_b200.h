@@ -57,6 +57,10 @@ typedef enum {
   KDA_ERR_CUDA = 10         /* another CUDA runtime error                     */
 } kda_status_t;
 
+/* KdaArgs.flags bits. */
+#define KDA_FLAG_FORCE_SIMT 1  /* chunkwise: use the CUDA-core kernel even where the
+                                  tensor-core kernel applies (cross-checking) */
+
 /* Arguments shared by both entry points. */
 typedef struct KdaArgs {
   int32_t abi_version;      /* must be KDA_B200_ABI_VERSION */
@@ -66,6 +70,7 @@ typedef struct KdaArgs {
   int32_t state_in_dtype;   /* dtype of state_in (ignored when NULL) */
   int32_t state_out_dtype;  /* dtype of state_out */
   float scale;              /* multiplier applied to q (K^-0.5 in the reference) */
+  int32_t flags;            /* KDA_FLAG_* bits, 0 by default */
   const void* q;     int64_t q_stride[4];
   const void* k;     int64_t k_stride[4];
   const void* v;     int64_t v_stride[4];
@@ -116,6 +121,13 @@ const char* kda_status_string(int status);
 /* 1 when `device` is an sm_100 GPU these kernels run on, 0 otherwise,
  * <0 on a CUDA error.  No reference counterpart. */
 int kda_device_supported(int device);
+
+/*
+ * Error word written by a kernel that abandoned its work after a bounded wait
+ * on the GPU ran out (0 = none); clear != 0 resets it.  Synchronises with the
+ * device.  <0 on a CUDA error.  No reference counterpart (diagnostic).
+ */
+int kda_device_error(int clear);
 
 /* sizeof(KdaArgs) as compiled, for FFI layout checks. */
 size_t kda_args_size(void);

@@ -36,6 +36,7 @@ KDA_ERR_CUDA = 10
 EXPORTED = (
     "kda_chunkwise_fwd",
     "kda_recurrent_fwd",
+    "kda_chunkwise_fwd_noalloc",
     "kda_chunkwise_workspace_bytes",
     "kda_chunkwise_path",
     "kda_status_string",
@@ -87,6 +88,8 @@ def _declare(lib):
     P = ctypes.POINTER(KdaArgs)
     lib.kda_chunkwise_fwd.argtypes = [P, ctypes.c_void_p]
     lib.kda_chunkwise_fwd.restype = ctypes.c_int
+    lib.kda_chunkwise_fwd_noalloc.argtypes = [P, ctypes.c_void_p]
+    lib.kda_chunkwise_fwd_noalloc.restype = ctypes.c_int
     lib.kda_recurrent_fwd.argtypes = [P, ctypes.c_void_p]
     lib.kda_recurrent_fwd.restype = ctypes.c_int
     lib.kda_chunkwise_workspace_bytes.argtypes = [P]

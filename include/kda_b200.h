@@ -102,6 +102,22 @@ int kda_chunkwise_fwd(const KdaArgs* args, void* stream);
 int kda_recurrent_fwd(const KdaArgs* args, void* stream);
 
 /*
+ * kda_chunkwise_fwd without any device allocation by anyone: the tensor-core
+ * path's scratch is a fixed 32 MiB array inside this library instead of a
+ * caller-allocated workspace (args->workspace is ignored).  For callers that
+ * cannot call cudaMalloc on their hot path -- a host that reserves all device
+ * memory up front, an engine plugin whose enqueue may not allocate, or a plain
+ * C caller without a device allocator.  The caller still provides o and
+ * state_out.  Returns KDA_ERR_WORKSPACE when kda_chunkwise_workspace_bytes()
+ * exceeds 32 MiB (B * H * ceil(T / 64) > 508 on the tensor-core path).  The
+ * first call on a device looks up the array's address (cudaGetSymbolAddress),
+ * so make it before any CUDA-graph capture; every GPU that loads the library
+ * holds the array until exit.  All calls share the array: calls whose kernels
+ * overlap on the GPU race.  No counterpart in the reference.
+ */
+int kda_chunkwise_fwd_noalloc(const KdaArgs* args, void* stream);
+
+/*
  * Device scratch bytes kda_chunkwise_fwd needs for `args` (0 = none).
  * No reference counterpart: the reference allocates its transients inside
  * torch (kda.py:131-138,148-149).

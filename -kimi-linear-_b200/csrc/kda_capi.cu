@@ -56,6 +56,14 @@ bool vec8_ok(const void* ptr, const int64_t* stride) {
   return true;
 }
 
+// 2 consecutive innermost elements at any row start are 2-element aligned.
+bool vec2_ok(const void* ptr, const int64_t* stride, int esize) {
+  if ((reinterpret_cast<uintptr_t>(ptr) % (uintptr_t)(2 * esize)) != 0) return false;
+  for (int d = 0; d < 3; ++d)
+    if (stride[d] % 2 != 0) return false;
+  return true;
+}
+
 int validate(const KdaArgs* a, bool chunkwise) {
   if (a == nullptr) return KDA_ERR_NULL_POINTER;
   if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
@@ -115,6 +123,10 @@ RecParams to_params(const KdaArgs* a) {
   p.v_vec16 = a->io_dtype != KDA_DTYPE_F32 && vec8_ok(a->v, a->v_stride);
   p.o_vec16 = a->io_dtype != KDA_DTYPE_F32 && vec8_ok(a->o, a->o_stride);
   p.force_simt = (a->flags & KDA_FLAG_FORCE_SIMT) != 0;
+  p.g_vec2 = vec2_ok(a->g, a->g_stride, 4);
+  p.qk_vec2 = vec2_ok(a->q, a->q_stride, elt_size(a->io_dtype)) &&
+              vec2_ok(a->k, a->k_stride, elt_size(a->io_dtype));
+  p.v_vec2 = vec2_ok(a->v, a->v_stride, elt_size(a->io_dtype));
   return p;
 }
 

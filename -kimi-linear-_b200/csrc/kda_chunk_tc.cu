@@ -11,9 +11,10 @@
 //      M = (I + L)^-1 Diag(beta)                             (kda.py:170-171)
 //      W = M (exp(gc) * K)                                   (kda.py:172)
 //      Qbar = s q exp(gc),  Kbar = exp(gc_last - gc) k,  d = exp(gc_last)
-//    and writes them as ONE 66,048-byte image per chunk whose byte layout is
-//    exactly the tcgen05 shared-memory operand layout the second kernel uses,
-//    so that kernel moves it with a single bulk (TMA-engine) copy.
+//    and writes them, with V converted to f16, as ONE 82,432-byte image per
+//    chunk whose byte layout is exactly the tcgen05 shared-memory operand
+//    layout the second kernel uses, so that kernel moves a chunk with two bulk
+//    (TMA-engine) copies: the shared operands and its own slice of V.
 //
 //    The decay products exp(gc_c - gc_i) are never formed pair by pair.  The
 //    chunk is split into four 16-row blocks; with the per-step decays
@@ -21,14 +22,15 @@
 //    product) and nb_c = exp(gc_nextblockstart - gc_c) (suffix product), both
 //    in (0, 1].  For a pair in different blocks the decay is
 //    ra_c * nb_i * (product of the whole-block decays in between): a dense
-//    16x16x128 tensor-core GEMM on pre-scaled operands (tf32 mma.sync), with
-//    no overflow possible.  Inside a diagonal block the decay is
+//    16x16x128 tensor-core GEMM on pre-scaled operands (tf32 mma.sync, the A
+//    fragments of a row block held in registers), with no overflow possible.  Inside a diagonal block the decay is
 //    ra_c * nb_i * exp(-Z_r) with Z_r the block's total decay; that factor is
 //    at most e^80 when the block is not "steep" (Z_r >= -80), which tf32 holds
 //    exactly.  Channels of a steep block are removed from that GEMM and their
 //    exact pair terms exp(gc_c - gc_i) are added separately (rare).
-//    (I + L)^-1 is a blocked forward substitution in fp32: 16x16 diagonal
-//    blocks by substitution, off-diagonal blocks M_rj = -D_r sum_t L_rt M_tj.
+//    (I + L)^-1 is a blocked forward substitution: 16x16 diagonal blocks by
+//    fp32 substitution, off-diagonal blocks M_rj = -D_r sum_t L_rt M_tj as
+//    3xTF32 tensor-core products (fp32-level accuracy).
 //
 // 2. state_kernel -- one CTA per (b, h, slice of VS value columns), walking the
 //    chunks in order with the fp32 state S[128, VS] resident in TMEM.  Per
@@ -57,13 +59,16 @@ namespace tc {
 
 constexpr int CH = 64;        // rows per chunk
 constexpr int KD = 128;       // head dim K of this path
-// chunk image (bytes); all operands f16, no-swizzle K-major core-matrix layout
-constexpr int IMG_A1 = 0;         // [-W; Qbar]  128 x 128, LBO 128, SBO 2048
-constexpr int IMG_A2 = 32768;     // [M; Aout]   128 x 64,  LBO 128, SBO 1024
-constexpr int IMG_A3 = 49152;     // Kbar^T      128 x 64,  LBO 128, SBO 1024
+// chunk image (bytes); all operands f16 in the no-swizzle core-matrix layout
+// (8 rows x 16 bytes per core matrix; LBO = stride along K, SBO = along M/N)
+constexpr int IMG_A1 = 0;         // [-W; Qbar]  128 x 128 K-major, LBO 128, SBO 2048
+constexpr int IMG_A2 = 32768;     // [M; Aout]   128 x 64  K-major, LBO 128, SBO 1024
+constexpr int IMG_A3 = 49152;     // Kbar^T      128 x 64  K-major, LBO 128, SBO 1024
 constexpr int IMG_D = 65536;      // d = exp(gc_last), fp32[128]
-constexpr int IMG_BYTES = 66048;
-constexpr int IMG_PAD = 66560;    // 65 KiB, keeps the next buffer 1 KiB aligned
+constexpr int IMG_SHARED = 66048; // bytes every value slice needs
+constexpr int IMG_V = 66048;      // V 64 x 128 MN-major, LBO 128, SBO 1024 (slice v0: +v0*128)
+constexpr int IMG_BYTES = 82432;
+constexpr int IMG_PAD = 66560;    // shared part rounded up to 1 KiB (stage layout)
 
 constexpr float kSteep = 80.f;                  // block decay beyond which exp(-Z) is unsafe
 constexpr uint64_t kWaitNs = 2000000000ull;     // bound on every mbarrier wait (2 s)
@@ -74,25 +79,82 @@ __device__ __forceinline__ int a1_off(int m, int k) {
 __device__ __forceinline__ int a2_off(int m, int k) {
   return (m >> 3) * 1024 + (k >> 3) * 128 + (m & 7) * 16 + (k & 7) * 2;
 }
+// MN-major B operand with K = 64 rows: offset(c, v)
+__device__ __forceinline__ int vb_off(int c, int v) {
+  return (v >> 3) * 1024 + (c >> 3) * 128 + (c & 7) * 16 + (v & 7) * 2;
+}
+
+// two consecutive innermost elements as fp32 (vector load when `vec`)
+template <typename T>
+__device__ __forceinline__ float2 ld2(const T* p, bool vec) {
+  if (vec) {
+    if constexpr (std::is_same<T, float>::value) return *reinterpret_cast<const float2*>(p);
+    if constexpr (std::is_same<T, __half>::value)
+      return __half22float2(*reinterpret_cast<const __half2*>(p));
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+      return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+  return make_float2(ld(p), ld(p + 1));
+}
+__device__ __forceinline__ void st_h2(uint8_t* base, int off, float a, float b) {
+  *reinterpret_cast<__half2*>(base + off) = __floats2half2_rn(a, b);
+}
 
 // ---------------------------------------------------------------------------
 // prep kernel
 // ---------------------------------------------------------------------------
-constexpr int AXP = 132;   // fp32 pitch of the Gram operand arrays (bank spread)
+constexpr int AXP = 144;   // fp32 pitch of the Gram operands: float4 fragment loads conflict-free
 constexpr int LMP = 68;    // fp32 pitch of L and M
+constexpr int TSP = 24;    // fp32 pitch of the per-warp 16x16 scratch (conflict-free B loads)
 constexpr int P_IMG = 0;
-constexpr int P_AXK = IMG_PAD;                         // k * ra          fp32 [64][132]
-constexpr int P_AXQ = P_AXK + CH * AXP * 4;            // s q * ra        fp32 [64][132]
-constexpr int P_YB = P_AXQ + CH * AXP * 4;             // k * nb          fp32 [64][132]
+constexpr int P_AXK = 82944;                           // k * ra          fp32 [64][144]
+constexpr int P_AXQ = P_AXK + CH * AXP * 4;            // s q * ra        fp32 [64][144]
+constexpr int P_YB = P_AXQ + CH * AXP * 4;             // k * nb          fp32 [64][144]
 constexpr int P_LM = P_YB + CH * AXP * 4;              // L               fp32 [64][68]
-constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4] fp32 [7][128]
-constexpr int P_BETA = P_FAC + 7 * KD * 4;             // beta            fp32 [64]
+constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4],Z[4],a0  [12][128]
+constexpr int P_BETA = P_FAC + 12 * KD * 4;            // beta            fp32 [64]
 constexpr int P_STEEP = P_BETA + CH * 4;               // steep bits      u32 [4][4]
 constexpr int PREP_SMEM = P_STEEP + 16 * 4;
+static_assert(P_AXK >= IMG_BYTES, "image staging");
 static_assert(PREP_SMEM <= 227 * 1024, "prep shared memory");
-// M (fp32, pitch LMP) reuses the k*ra array and the inversion scratch the
-// q*ra array once the Gram is done
+// M (fp32, pitch LMP) reuses the k*ra array once the Gram is done, and the
+// inversion scratch the q*ra array
 constexpr int PREP_THREADS = 256;
+
+// 3xTF32 split: x ~= hi + lo with both parts exact in tf32
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = ptx::f32_to_tf32(x);
+  lo = ptx::f32_to_tf32(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma3_tf32(float* acc, const uint32_t* ah, const uint32_t* al,
+                                          const uint32_t* bh, const uint32_t* bl) {
+  ptx::mma_tf32_16x8x8(acc, al, bh);
+  ptx::mma_tf32_16x8x8(acc, ah, bl);
+  ptx::mma_tf32_16x8x8(acc, ah, bh);
+}
+
+// C[16x16] = A[16 x 8*ksteps] * B[8*ksteps x 16] in ~fp32 precision (3xTF32);
+// A(row, k) = Ab[row*lda + k], B(k, col) = Bb[k*ldb + col]; result in acc[2][4]
+// (n-tile nt: rows gid / gid+8, cols 8nt + 2tig (+1))
+__device__ __forceinline__ void gemm16_3xtf32(float (*acc)[4], const float* Ab, int lda,
+                                              const float* Bb, int ldb, int ksteps, int lane) {
+  const int gid = lane >> 2, tig = lane & 3;
+  for (int ks = 0; ks < ksteps; ++ks) {
+    const int k0 = 8 * ks;
+    uint32_t ah[4], al[4];
+    split_tf32(Ab[gid * lda + k0 + tig], ah[0], al[0]);
+    split_tf32(Ab[(gid + 8) * lda + k0 + tig], ah[1], al[1]);
+    split_tf32(Ab[gid * lda + k0 + tig + 4], ah[2], al[2]);
+    split_tf32(Ab[(gid + 8) * lda + k0 + tig + 4], ah[3], al[3]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      uint32_t bh[2], bl[2];
+      split_tf32(Bb[(k0 + tig) * ldb + 8 * nt + gid], bh[0], bl[0]);
+      split_tf32(Bb[(k0 + tig + 4) * ldb + 8 * nt + gid], bh[1], bl[1]);
+      mma3_tf32(acc[nt], ah, al, bh, bl);
+    }
+  }
+}
 
 template <typename TIO>
 __global__ void __launch_bounds__(PREP_THREADS, 1)
@@ -106,7 +168,9 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   float* P02 = reinterpret_cast<float*>(sm + P_FAC);
   float* P03 = P02 + KD;
   float* P13 = P03 + KD;
-  float* Ef = P13 + KD;                                   // [4][128]
+  float* Ef = P13 + KD;            // [4][128]  exp(-Z_r), 0 for steep channels
+  float* Zs = Ef + 4 * KD;         // [4][128]  block decays Z_r
+  float* A0 = Zs + 4 * KD;         // [128]     exp(g of row 0)
   float* sbeta = reinterpret_cast<float*>(sm + P_BETA);
   uint32_t* steep = reinterpret_cast<uint32_t*>(sm + P_STEEP);
 
@@ -118,6 +182,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   const float s = p.scale;
   const TIO* qb = static_cast<const TIO*>(p.q) + b * p.q_s[0] + h * p.q_s[2];
   const TIO* kb = static_cast<const TIO*>(p.k) + b * p.k_s[0] + h * p.k_s[2];
+  const TIO* vb = static_cast<const TIO*>(p.v) + b * p.v_s[0] + h * p.v_s[2];
   const float* gb = p.g + b * p.g_s[0] + h * p.g_s[2];
   const float* bb = p.beta + b * p.b_s[0] + h * p.b_s[2];
 
@@ -127,118 +192,154 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     reinterpret_cast<int4*>(img + IMG_A2 + 8192)[i] = make_int4(0, 0, 0, 0);
   if (tid < 16) steep[tid] = 0u;
   if (tid < CH) sbeta[tid] = (tid < nvalid) ? bb[(int64_t)(t0 + tid) * p.b_s[1]] : 0.f;
-  __syncthreads();
 
-  // ---- 1. per channel: decays, factors, decayed operands -------------------
+  // ---- 1. per (16-row block r, channel pair): decays and decayed operands --
+  const int r = tid >> 6, k0 = 2 * (tid & 63);
+  float2 al[17];                    // al[i] = exp(g) of row 16r + i (i >= 1)
+  float2 zr;
   {
-    const int k = tid & (KD - 1), half = tid >> 7;
-    float gv[CH];
+    float2 gr[17];
 #pragma unroll
-    for (int c = 0; c < CH; ++c)
-      gv[c] = (c < nvalid) ? gb[(int64_t)(t0 + c) * p.g_s[1] + k] : 0.f;
-    float Zp[4], eZ[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int hi = (r < 3) ? 16 * (r + 1) : CH - 1;
-      float z = 0.f;
-#pragma unroll
-      for (int t = 16 * r + 1; t <= hi; ++t) z += gv[t];
-      Zp[r] = z;
-      eZ[r] = expf(z);
+    for (int i = 0; i < 17; ++i) {
+      const int c = 16 * r + i;
+      gr[i] = (c < nvalid) ? ld2(gb + (int64_t)(t0 + c) * p.g_s[1] + k0, p.g_vec2)
+                           : make_float2(0.f, 0.f);
     }
-    const float a0 = expf(gv[0]);
-    float Bf[4], Af[4];
-    Bf[0] = a0;
-    Bf[1] = Bf[0] * eZ[0];
-    Bf[2] = Bf[1] * eZ[1];
-    Bf[3] = Bf[2] * eZ[2];
-    Af[3] = 1.f;
-    Af[2] = eZ[3];
-    Af[1] = eZ[2] * eZ[3];
-    Af[0] = eZ[1] * Af[1];
-    if (half == 0) {
-      P02[k] = eZ[1];
-      P03[k] = eZ[1] * eZ[2];
-      P13[k] = eZ[2];
+    // Z_r = sum of g over rows 16r+1 .. 16r+16 (..63 for the last block)
+    zr = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const bool st = Zp[r] < -kSteep;
-        Ef[r * KD + k] = st ? 0.f : expf(-Zp[r]);
-        if (st) atomicOr(&steep[r * 4 + (k >> 5)], 1u << (k & 31));
-      }
-      reinterpret_cast<float*>(img + IMG_D)[k] = Bf[3] * eZ[3];   // exp(gc_last)
+    for (int i = 1; i < 17; ++i) {
+      if (i == 16 && r == 3) break;
+      zr.x += gr[i].x;
+      zr.y += gr[i].y;
     }
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      if ((r >> 1) != half) continue;
-      const int hi = (r < 3) ? 16 * (r + 1) : CH - 1;
-      float al[17];
+    for (int i = 1; i < 17; ++i) al[i] = make_float2(__expf(gr[i].x), __expf(gr[i].y));
+    if (r == 3) al[16] = make_float2(1.f, 1.f);
+    Zs[r * KD + k0] = zr.x;
+    Zs[r * KD + k0 + 1] = zr.y;
+    if (r == 0) {
+      A0[k0] = expf(gr[0].x);
+      A0[k0 + 1] = expf(gr[0].y);
+    }
+  }
+  __syncthreads();
+  {
+    float eZx[4], eZy[4];
 #pragma unroll
-      for (int i = 1; i <= 16; ++i) al[i] = (16 * r + i <= hi) ? expf(gv[16 * r + i]) : 1.f;
-      float ra[16], nb[16];
-      ra[0] = 1.f;
+    for (int j = 0; j < 4; ++j) {
+      eZx[j] = expf(Zs[j * KD + k0]);
+      eZy[j] = expf(Zs[j * KD + k0 + 1]);
+    }
+    float bfx = A0[k0], bfy = A0[k0 + 1];        // exp(gc at the block start)
+    float afx = 1.f, afy = 1.f;                  // exp(gc_last - gc at the next block start)
 #pragma unroll
-      for (int i = 1; i < 16; ++i) ra[i] = ra[i - 1] * al[i];
-      nb[15] = al[16];
+    for (int j = 0; j < 4; ++j) {
+      if (j < r) { bfx *= eZx[j]; bfy *= eZy[j]; }
+      if (j > r) { afx *= eZx[j]; afy *= eZy[j]; }
+    }
+    if (r == 0) {
+      P02[k0] = eZx[1];                P02[k0 + 1] = eZy[1];
+      P03[k0] = eZx[1] * eZx[2];       P03[k0 + 1] = eZy[1] * eZy[2];
+      P13[k0] = eZx[2];                P13[k0 + 1] = eZy[2];
+      float* dimg = reinterpret_cast<float*>(img + IMG_D);
+      dimg[k0] = A0[k0] * eZx[0] * eZx[1] * eZx[2] * eZx[3];
+      dimg[k0 + 1] = A0[k0 + 1] * eZy[0] * eZy[1] * eZy[2] * eZy[3];
+    }
+    {
+      const bool stx = zr.x < -kSteep, sty = zr.y < -kSteep;
+      Ef[r * KD + k0] = stx ? 0.f : expf(-zr.x);
+      Ef[r * KD + k0 + 1] = sty ? 0.f : expf(-zr.y);
+      const uint32_t bits = (stx ? 1u : 0u) | (sty ? 2u : 0u);
+      if (bits) atomicOr(&steep[r * 4 + (k0 >> 5)], bits << (k0 & 31));
+    }
+    // ra: prefix products from the block start; nb: suffix products to the next block start
+    float2 ra[16], nb[16];
+    ra[0] = make_float2(1.f, 1.f);
 #pragma unroll
-      for (int i = 14; i >= 0; --i) nb[i] = nb[i + 1] * al[i + 1];
+    for (int i = 1; i < 16; ++i) ra[i] = make_float2(ra[i - 1].x * al[i].x, ra[i - 1].y * al[i].y);
+    nb[15] = al[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int c = 16 * r + i;
-        float qv = 0.f, kv = 0.f;
-        if (c < nvalid) {
-          qv = ld(qb + (int64_t)(t0 + c) * p.q_s[1] + k);
-          kv = ld(kb + (int64_t)(t0 + c) * p.k_s[1] + k);
-        }
-        const float qs = qv * s;
-        const float eg = Bf[r] * ra[i];                   // exp(gc_c)
-        *reinterpret_cast<__half*>(img + IMG_A1 + a1_off(64 + c, k)) = __float2half_rn(qs * eg);
-        *reinterpret_cast<__half*>(img + IMG_A1 + a1_off(c, k)) = __float2half_rn(kv * eg);
-        *reinterpret_cast<__half*>(img + IMG_A3 + a2_off(k, c)) =
-            __float2half_rn(kv * nb[i] * Af[r]);            // exp(gc_last - gc_c) k
-        Axk[c * AXP + k] = kv * ra[i];
-        Axq[c * AXP + k] = qs * ra[i];
-        Yb[c * AXP + k] = kv * nb[i];
+    for (int i = 14; i >= 0; --i)
+      nb[i] = make_float2(nb[i + 1].x * al[i + 1].x, nb[i + 1].y * al[i + 1].y);
+    float kbx[16], kby[16];         // Kbar for the transposed store
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int c = 16 * r + i;
+      float2 qv = make_float2(0.f, 0.f), kv = qv, vv = qv;
+      if (c < nvalid) {
+        qv = ld2(qb + (int64_t)(t0 + c) * p.q_s[1] + k0, p.qk_vec2);
+        kv = ld2(kb + (int64_t)(t0 + c) * p.k_s[1] + k0, p.qk_vec2);
+        vv = ld2(vb + (int64_t)(t0 + c) * p.v_s[1] + k0, p.v_vec2);
       }
+      const float qsx = qv.x * s, qsy = qv.y * s;
+      const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;     // exp(gc_c)
+      st_h2(img, IMG_A1 + a1_off(64 + c, k0), qsx * egx, qsy * egy);   // Qbar
+      st_h2(img, IMG_A1 + a1_off(c, k0), kv.x * egx, kv.y * egy);      // Ktilde
+      st_h2(img, IMG_V + vb_off(c, k0), vv.x, vv.y);                   // V (f16)
+      kbx[i] = kv.x * nb[i].x * afx;                                   // Kbar
+      kby[i] = kv.y * nb[i].y * afy;
+      *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
+      *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
+      *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      st_h2(img, IMG_A3 + a2_off(k0, 16 * r + i), kbx[i], kbx[i + 1]);
+      st_h2(img, IMG_A3 + a2_off(k0 + 1, 16 * r + i), kby[i], kby[i + 1]);
     }
   }
   __syncthreads();
 
-  // ---- 2. Gram blocks L and Aout (tf32 mma.sync, fp32 accumulate) ----------
+  // ---- 2. Gram blocks: warp = (row block rr, type); A fragments in registers.
+  // The K order inside each 16-channel group is permuted (sums are order-free)
+  // so every fragment element pair comes from one float4 load.
   {
     const int gid = lane >> 2, tig = lane & 3;
-    for (int task = warp; task < 20; task += PREP_THREADS / 32) {
-      const int type = task / 10;                     // 0: L (x = k), 1: Aout (x = s q)
-      int j = task % 10, r = 0;
-      while (j > r) { j -= r + 1; ++r; }
-      const float* Ax = type ? Axq : Axk;
-      const float* f = nullptr;                       // per-channel factor on the B side
-      if (j == r) f = Ef + r * KD;
-      else if (r - j == 2) f = (j == 0) ? P02 : P13;
-      else if (r - j == 3) f = P03;
+    const int rr = warp & 3, type = warp >> 2;          // type 0: L (x = k), 1: Aout (x = s q)
+    const float* Ax = type ? Axq : Axk;
+    uint32_t af[8][2][4];                               // [16-channel group][k-step][frag]
+    float4 arow0[8], arow1[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      arow0[g] = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid) * AXP + 16 * g + 4 * tig);
+      arow1[g] = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid + 8) * AXP + 16 * g + 4 * tig);
+    }
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      af[g][0][0] = ptx::f32_to_tf32(arow0[g].x);
+      af[g][0][1] = ptx::f32_to_tf32(arow1[g].x);
+      af[g][0][2] = ptx::f32_to_tf32(arow0[g].y);
+      af[g][0][3] = ptx::f32_to_tf32(arow1[g].y);
+      af[g][1][0] = ptx::f32_to_tf32(arow0[g].z);
+      af[g][1][1] = ptx::f32_to_tf32(arow1[g].z);
+      af[g][1][2] = ptx::f32_to_tf32(arow0[g].w);
+      af[g][1][3] = ptx::f32_to_tf32(arow1[g].w);
+    }
+    for (int j = 0; j <= rr; ++j) {
+      const float* f = nullptr;                         // per-channel factor on the B side
+      if (j == rr) f = Ef + rr * KD;
+      else if (rr - j == 2) f = (j == 0) ? P02 : P13;
+      else if (rr - j == 3) f = P03;
       float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      const float* ar0 = Ax + (16 * r + gid) * AXP;
-      const float* ar1 = ar0 + 8 * AXP;
-      const float* br0 = Yb + (16 * j + gid) * AXP;
-      const float* br1 = br0 + 8 * AXP;
-#pragma unroll 4
-      for (int k0 = 0; k0 < KD; k0 += 8) {
-        const uint32_t a[4] = {ptx::f32_to_tf32(ar0[k0 + tig]), ptx::f32_to_tf32(ar1[k0 + tig]),
-                               ptx::f32_to_tf32(ar0[k0 + tig + 4]),
-                               ptx::f32_to_tf32(ar1[k0 + tig + 4])};
-        const float f0 = f ? f[k0 + tig] : 1.f, f1 = f ? f[k0 + tig + 4] : 1.f;
-        const uint32_t b0[2] = {ptx::f32_to_tf32(br0[k0 + tig] * f0),
-                                ptx::f32_to_tf32(br0[k0 + tig + 4] * f1)};
-        const uint32_t b1[2] = {ptx::f32_to_tf32(br1[k0 + tig] * f0),
-                                ptx::f32_to_tf32(br1[k0 + tig + 4] * f1)};
-        ptx::mma_tf32_16x8x8(acc[0], a, b0);
-        ptx::mma_tf32_16x8x8(acc[1], a, b1);
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const int kc = 16 * g + 4 * tig;
+        const float4 fv = f ? *reinterpret_cast<const float4*>(f + kc) : make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float4 y = *reinterpret_cast<const float4*>(Yb + (16 * j + 8 * nt + gid) * AXP + kc);
+          const uint32_t b0[2] = {ptx::f32_to_tf32(y.x * fv.x), ptx::f32_to_tf32(y.y * fv.y)};
+          const uint32_t b1[2] = {ptx::f32_to_tf32(y.z * fv.z), ptx::f32_to_tf32(y.w * fv.w)};
+          ptx::mma_tf32_16x8x8(acc[nt], af[g][0], b0);
+          ptx::mma_tf32_16x8x8(acc[nt], af[g][1], b1);
+        }
       }
-      if (j == r) {
-        // exact pair terms of the steep channels of this diagonal block
+      if (j == rr) {
+        // exact pair terms of the steep channels of this diagonal block (rare)
 #pragma unroll 1
         for (int w4 = 0; w4 < 4; ++w4) {
-          uint32_t m = steep[r * 4 + w4];
+          uint32_t m = steep[rr * 4 + w4];
           while (m) {
             const int kk = w4 * 32 + __ffs(m) - 1;
             m &= m - 1;
@@ -246,7 +347,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
             pre[0] = 0.f;
 #pragma unroll
             for (int i = 1; i < 16; ++i) {
-              const int c = 16 * r + i;
+              const int c = 16 * rr + i;
               pre[i] = pre[i - 1] + ((c < nvalid) ? gb[(int64_t)(t0 + c) * p.g_s[1] + kk] : 0.f);
             }
 #pragma unroll
@@ -254,7 +355,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int rl = gid + 8 * (e >> 1), cl = 8 * nt + 2 * tig + (e & 1);
-                const int c = 16 * r + rl, i = 16 * r + cl;
+                const int c = 16 * rr + rl, i = 16 * rr + cl;
                 if (cl <= rl && c < nvalid) {
                   const float xr = type ? s * ld(qb + (int64_t)(t0 + c) * p.q_s[1] + kk)
                                         : ld(kb + (int64_t)(t0 + c) * p.k_s[1] + kk);
@@ -269,7 +370,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int row = 16 * r + gid + 8 * (e >> 1);
+          const int row = 16 * rr + gid + 8 * (e >> 1);
           const int col = 16 * j + 8 * nt + 2 * tig + (e & 1);
           const float v = acc[nt][e];
           if (type == 0) {
@@ -282,11 +383,11 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   }
   __syncthreads();
 
-  // ---- 3. M = (I + L)^-1 Diag(beta), blocked forward substitution (fp32) ---
+  // ---- 3. M = (I + L)^-1 Diag(beta): blocked forward substitution ----------
   float* Mm = Axk;                     // pitch LMP
-  float* Ts = Axq;                     // per-warp 16x17 scratch
-  if (warp < 4) {
-    const int r = warp;
+  float* Ts = Axq;                     // per-warp 16 x TSP scratch
+  if (warp < 4) {                      // diagonal blocks by substitution (fp32)
+    const int rb = warp;
     if (lane < 16) {
       const int j = lane;
       float x[16];
@@ -294,11 +395,11 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       for (int c = 0; c < 16; ++c) {
         float acc = (c == j) ? 1.f : 0.f;
 #pragma unroll
-        for (int i = 0; i < c; ++i) acc = fmaf(-Lm[(16 * r + c) * LMP + 16 * r + i], x[i], acc);
+        for (int i = 0; i < c; ++i) acc = fmaf(-Lm[(16 * rb + c) * LMP + 16 * rb + i], x[i], acc);
         x[c] = acc;
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) Mm[(16 * r + c) * LMP + 16 * r + j] = x[c];
+      for (int c = 0; c < 16; ++c) Mm[(16 * rb + c) * LMP + 16 * rb + j] = x[c];
     }
   } else {
     for (int idx = tid - 128; idx < CH * CH; idx += 128) {
@@ -307,32 +408,36 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     }
   }
   __syncthreads();
+  // off-diagonal blocks M_rj = -D_r sum_{t=j}^{r-1} L_rt M_tj, by distance r - j
   for (int dist = 1; dist <= 3; ++dist) {
     if (warp < 4 - dist) {
-      const int j = warp, r = warp + dist;
-      float* T = Ts + warp * (16 * 17);
-      for (int o = lane; o < 256; o += 32) {
-        const int row = o >> 4, col = o & 15;
-        float acc = 0.f;
-        for (int cp = 16 * j; cp < 16 * r; ++cp)
-          acc = fmaf(Lm[(16 * r + row) * LMP + cp], Mm[cp * LMP + 16 * j + col], acc);
-        T[row * 17 + col] = acc;
-      }
+      const int j = warp, rb = warp + dist;
+      const int gid = lane >> 2, tig = lane & 3;
+      float tacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      gemm16_3xtf32(tacc, Lm + (16 * rb) * LMP + 16 * j, LMP, Mm + (16 * j) * LMP + 16 * j, LMP,
+                    2 * dist, lane);
+      float* T = Ts + warp * (16 * TSP);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          T[(gid + 8 * (e >> 1)) * TSP + 8 * nt + 2 * tig + (e & 1)] = tacc[nt][e];
       __syncwarp();
-      for (int o = lane; o < 256; o += 32) {
-        const int row = o >> 4, col = o & 15;
-        float acc = 0.f;
-        for (int i = 0; i <= row; ++i)
-          acc = fmaf(Mm[(16 * r + row) * LMP + 16 * r + i], T[i * 17 + col], acc);
-        Mm[(16 * r + row) * LMP + 16 * j + col] = -acc;
-      }
+      float macc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      gemm16_3xtf32(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, T, TSP, 2, lane);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          Mm[(16 * rb + gid + 8 * (e >> 1)) * LMP + 16 * j + 8 * nt + 2 * tig + (e & 1)] =
+              -macc[nt][e];
     }
     __syncthreads();
   }
-  for (int idx = tid; idx < CH * CH; idx += PREP_THREADS) {
-    const int row = idx >> 6, col = idx & 63;
-    *reinterpret_cast<__half*>(img + IMG_A2 + a2_off(row, col)) =
-        __float2half_rn(Mm[row * LMP + col] * sbeta[col]);
+  for (int idx = tid; idx < CH * CH / 2; idx += PREP_THREADS) {
+    const int row = idx >> 5, col = 2 * (idx & 31);
+    st_h2(img, IMG_A2 + a2_off(row, col), Mm[row * LMP + col] * sbeta[col],
+          Mm[row * LMP + col + 1] * sbeta[col + 1]);
   }
   __syncthreads();
 
@@ -366,8 +471,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       for (int hr = 0; hr < 2; ++hr) {
         const int row = 16 * rb + gid + 8 * hr;
         const int col = 64 * ch + 8 * nt + 2 * tig;
-        *reinterpret_cast<__half2*>(img + IMG_A1 + a1_off(row, col)) =
-            __floats2half2_rn(-acc[nt][2 * hr], -acc[nt][2 * hr + 1]);
+        st_h2(img, IMG_A1 + a1_off(row, col), -acc[nt][2 * hr], -acc[nt][2 * hr + 1]);
       }
   }
   __syncthreads();
@@ -385,12 +489,13 @@ template <int VS>
 struct StateCfg {
   static constexpr int NCOL = VS <= 16 ? 64 : (VS <= 32 ? 128 : (VS <= 64 ? 256 : 512));
   static constexpr int R1 = 0, R2 = VS, R3 = 2 * VS;
-  static constexpr int VT_BYTES = CH * VS * 2;                 // V tile, K = 64 rows
+  static constexpr int VT_BYTES = CH * VS * 2;                 // V slice, K = 64 rows
   static constexpr int STAGE = IMG_PAD + ((VT_BYTES + 1023) / 1024) * 1024;
   static constexpr int SB_OFF = 2 * STAGE;                     // S  (K = 128) f16
   static constexpr int PB_OFF = SB_OFF + KD * VS * 2;          // P  (K = 64)  f16
   static constexpr int BAR_OFF = PB_OFF + CH * VS * 2;
   static constexpr int SMEM = BAR_OFF + 64;
+  static constexpr uint32_t TX = IMG_SHARED + VT_BYTES;        // bytes per chunk
   static_assert(SMEM <= 227 * 1024, "state shared memory");
 };
 
@@ -406,29 +511,16 @@ __device__ __forceinline__ int4 pack8_f16(const float* x) {
   return r;
 }
 
-// V tile of chunk n (rows t = 64n + c, columns v0 .. v0+VS) as the f16
-// MN-major B operand: offset(c, v) = (v/8)*1024 + (c/8)*128 + (c%8)*16 + (v%8)*2
-template <int VS, typename TIO>
-__device__ __forceinline__ void load_vtile(uint8_t* vt, const ChunkParams& p, int b, int h,
-                                           int v0, int n) {
-  constexpr int GPR = VS / 8;
-  for (int piece = threadIdx.x; piece < CH * GPR; piece += 128) {
-    const int c = piece / GPR, gv = piece % GPR;
-    const int t = n * CH + c;
-    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (t < p.T) {
-      const TIO* src = static_cast<const TIO*>(p.v) + b * p.v_s[0] + (int64_t)t * p.v_s[1] +
-                       h * p.v_s[2] + v0 + 8 * gv;
-      if (p.v_vec16) {
-        ld4(src, *reinterpret_cast<float(*)[4]>(x));
-        ld4(src + 4, *reinterpret_cast<float(*)[4]>(x + 4));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = ld(src + e);
-      }
-    }
-    *reinterpret_cast<int4*>(vt + gv * 1024 + (c >> 3) * 128 + (c & 7) * 16) = pack8_f16(x);
-  }
+__device__ __forceinline__ void named_barrier_64() {
+  asm volatile("bar.sync 1, 64;" ::: "memory");
+}
+
+template <int VS>
+__device__ __forceinline__ void fetch_chunk(uint8_t* stg, const uint8_t* img_g, int v0,
+                                            uint64_t* bar) {
+  ptx::mbar_arrive_expect_tx(bar, StateCfg<VS>::TX);
+  ptx::bulk_g2s(stg, img_g, IMG_SHARED, bar);
+  ptx::bulk_g2s(stg + IMG_PAD, img_g + IMG_V + v0 * 128, StateCfg<VS>::VT_BYTES, bar);
 }
 
 template <int VS, typename TIO, typename TSI, typename TSO>
@@ -440,9 +532,10 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* Sb = sm + Cfg::SB_OFF;
   uint8_t* Pb = sm + Cfg::PB_OFF;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [2]
-  uint64_t* mbar = full + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [2] chunk images
+  uint64_t* mbarA = full + 2;      // first MMA batch of a chunk done (one phase per chunk)
+  uint64_t* mbarB = full + 3;      // second MMA batch of a chunk done (one phase per chunk)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -459,7 +552,8 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   if (tid == 0) {
     ptx::mbar_init(&full[0], 1);
     ptx::mbar_init(&full[1], 1);
-    ptx::mbar_init(mbar, 1);
+    ptx::mbar_init(mbarA, 1);
+    ptx::mbar_init(mbarB, 1);
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
@@ -473,8 +567,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   uint32_t pending = 0, pend_par = 0;
   if (tid == 0) {
     for (int sg = 0; sg < 2 && sg < NT; ++sg) {
-      ptx::mbar_arrive_expect_tx(&full[sg], IMG_BYTES);
-      ptx::bulk_g2s(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, IMG_BYTES, &full[sg]);
+      fetch_chunk<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
       pending |= 1u << sg;
     }
   }
@@ -492,19 +585,18 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     ptx::tmem_st<CW>(tlane + Cfg::R3 + pc * CW, srow);
   }
   ptx::tmem_wait_st();
-  load_vtile<VS, TIO>(sm + IMG_PAD, p, b, h, v0, 0);
 
   bool aborted = false;
   for (int n = 0; n < NT; ++n) {
     const int sg = n & 1;
     uint8_t* stg = sm + sg * Cfg::STAGE;
     uint8_t* vt = stg + IMG_PAD;
-    if (tid == 0) {
-      if (ptx::mbar_wait(&full[sg], (n >> 1) & 1, kWaitNs)) pending &= ~(1u << sg);
-      else *abort_flag = 1;
+    // every thread waits for image n itself (bounded)
+    if (ptx::mbar_wait(&full[sg], (n >> 1) & 1, kWaitNs)) {
+      if (tid == 0) pending &= ~(1u << sg);
+    } else {
+      *abort_flag = 1;
     }
-    __syncthreads();                                       // (1) image n in smem
-    if (*abort_flag) { aborted = true; break; }
     {
       // S -> f16 B operand (MN-major, K = 128): offset(k, v) = (v/8)*2048 + (k/8)*128 + (k%8)*16
       // and R3 <- d * S, in pieces of CW columns (register budget)
@@ -526,7 +618,8 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     }
     ptx::fence_proxy_async_smem();
     ptx::tc_fence_before();
-    __syncthreads();                                       // (2) Sb, V tile, d*S ready
+    __syncthreads();                                       // Sb and d*S ready
+    if (*abort_flag) { aborted = true; break; }
     if (tid == 0) {
       ptx::tc_fence_after();
       const uint32_t a2 = ptx::smem_u32(stg + IMG_A2), a1 = ptx::smem_u32(stg + IMG_A1);
@@ -539,14 +632,16 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
       for (int ks = 0; ks < 8; ++ks)                       // R1 = [-W; Qbar] S
         ptx::mma_f16_ss(tbase + Cfg::R1, ptx::sdesc(a1 + 256 * ks, 128, 2048),
                         ptx::sdesc(sb + 256 * ks, 128, 2048), IDESC, ks > 0);
-      ptx::tc_commit(mbar);
+      ptx::tc_commit(mbarA);
     }
-    if (n + 1 < NT) load_vtile<VS, TIO>(sm + (sg ^ 1) * Cfg::STAGE + IMG_PAD, p, b, h, v0, n + 1);
-    if (tid == 0 && !ptx::mbar_wait(mbar, 0, kWaitNs)) *abort_flag = 1;
-    __syncthreads();                                       // (3) R1, R2 ready
-    if (*abort_flag) { aborted = true; break; }
-    ptx::tc_fence_after();
+    // Warps 0-1 consume the first MMA batch; warps 2-3 only need the second.
+    // Each batch has its own barrier completing once per chunk, so the phase a
+    // thread waits for has parity n & 1 and can never be lapped: the next
+    // phase of either barrier needs the next chunk's CTA barrier.
+    const uint32_t par = static_cast<uint32_t>(n & 1);
     if (warp < 2) {                                        // P = U - W S, rows c = tid
+      if (!ptx::mbar_wait(mbarA, par, kWaitNs)) *abort_flag = 1;
+      ptx::tc_fence_after();
 #pragma unroll 1
       for (int pc = 0; pc < NP; ++pc) {
         float u[CW], w[CW];
@@ -560,36 +655,32 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
           *reinterpret_cast<int4*>(Pb + (pc * (CW / 8) + g8) * 1024 + (tid >> 3) * 128 +
                                    (tid & 7) * 16) = pack8_f16(u + 8 * g8);
       }
-    }
-    ptx::fence_proxy_async_smem();
-    ptx::tc_fence_before();
-    __syncthreads();                                       // (4) P ready
-    if (tid == 0) {
-      ptx::tc_fence_after();
-      const uint32_t a2 = ptx::smem_u32(stg + IMG_A2), a3 = ptx::smem_u32(stg + IMG_A3);
-      const uint32_t pb = ptx::smem_u32(Pb);
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      named_barrier_64();                                  // P ready (warps 0-1)
+      if (tid == 0) {
+        ptx::tc_fence_after();
+        const uint32_t a2 = ptx::smem_u32(stg + IMG_A2), a3 = ptx::smem_u32(stg + IMG_A3);
+        const uint32_t pb = ptx::smem_u32(Pb);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)                       // R1 += [M; Aout] P
-        ptx::mma_f16_ss(tbase + Cfg::R1, ptx::sdesc(a2 + 256 * ks, 128, 1024),
-                        ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
+        for (int ks = 0; ks < 4; ++ks)                     // R3 += Kbar^T P (next state first)
+          ptx::mma_f16_ss(tbase + Cfg::R3, ptx::sdesc(a3 + 256 * ks, 128, 1024),
+                          ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)                       // R3 += Kbar^T P
-        ptx::mma_f16_ss(tbase + Cfg::R3, ptx::sdesc(a3 + 256 * ks, 128, 1024),
-                        ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
-      ptx::tc_commit(mbar);
-      if (!ptx::mbar_wait(mbar, 1, kWaitNs)) {
-        *abort_flag = 1;
-      } else if (n + 2 < NT) {                             // stage free: fetch chunk n+2
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive_expect_tx(&full[sg], IMG_BYTES);
-        ptx::bulk_g2s(stg, wsh + (size_t)(n + 2) * IMG_BYTES, IMG_BYTES, &full[sg]);
-        pending |= 1u << sg;
-        pend_par = (pend_par & ~(1u << sg)) | ((((n + 2) >> 1) & 1u) << sg);
+        for (int ks = 0; ks < 4; ++ks)                     // R1 += [M; Aout] P
+          ptx::mma_f16_ss(tbase + Cfg::R1, ptx::sdesc(a2 + 256 * ks, 128, 1024),
+                          ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
+        ptx::tc_commit(mbarB);
       }
     }
-    __syncthreads();                                       // (5) O and next S ready
-    if (*abort_flag) { aborted = true; break; }
+    if (!ptx::mbar_wait(mbarB, par, kWaitNs)) *abort_flag = 1;
     ptx::tc_fence_after();
+    if (tid == 0 && n + 2 < NT && !*abort_flag) {          // stage free: fetch chunk n+2
+      ptx::fence_proxy_async_smem();
+      fetch_chunk<VS>(stg, wsh + (size_t)(n + 2) * IMG_BYTES, v0, &full[sg]);
+      pending |= 1u << sg;
+      pend_par = (pend_par & ~(1u << sg)) | ((((n + 2) >> 1) & 1u) << sg);
+    }
     if (warp >= 2) {                                       // O rows c = tid - 64
       const int t = n * CH + (tid - 64);
       TIO* dst = static_cast<TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] +
@@ -615,7 +706,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   }
 
   __syncthreads();
-  if (!aborted) {
+  if (!aborted && !*abort_flag) {
     ptx::tc_fence_after();
     TSO* dst = static_cast<TSO*>(p.state_out) + b * p.so_s[0] + h * p.so_s[1] +
                (int64_t)tid * p.so_s[2] + v0;
@@ -713,7 +804,7 @@ cudaError_t launch_tc1(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
 bool chunk_tc_supported(const ChunkParams& p) {
   if (p.force_simt) return false;
   if (p.io_dtype != KDA_DTYPE_F16 && p.io_dtype != KDA_DTYPE_BF16) return false;
-  if (p.K != tc::KD || p.T < 1 || p.V % 16 != 0) return false;
+  if (p.K != tc::KD || p.V != tc::KD || p.T < 1) return false;
   return tc::pick_vs(p) != 0;
 }
 

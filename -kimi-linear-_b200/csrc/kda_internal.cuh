@@ -25,6 +25,8 @@ struct RecParams {
   bool state_vec, state_out_vec, o_vec;
   // 16-byte access is legal for 8 consecutive 16-bit v / o elements
   bool v_vec16, o_vec16;
+  // 2-element access is legal (g: 8 bytes; q, k and v: 4 bytes)
+  bool g_vec2, qk_vec2, v_vec2;
   // run the CUDA-core chunkwise kernel even where the tensor-core one applies
   bool force_simt;
 };

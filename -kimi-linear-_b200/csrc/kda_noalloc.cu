@@ -28,8 +28,8 @@
 namespace kda {
 namespace {
 
-// 32 MiB: enough for B * H * ceil(T / 64) <= 508 chunk-heads on the
-// tensor-core path (66,048 bytes each), e.g. 16 heads x 2,032 tokens.
+// 32 MiB: enough for B * H * ceil(T / 64) <= 407 chunk-heads on the
+// tensor-core path (82,432 bytes each), e.g. 16 heads x 1,600 tokens.
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

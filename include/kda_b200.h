@@ -109,7 +109,7 @@ int kda_recurrent_fwd(const KdaArgs* args, void* stream);
  * memory up front, an engine plugin whose enqueue may not allocate, or a plain
  * C caller without a device allocator.  The caller still provides o and
  * state_out.  Returns KDA_ERR_WORKSPACE when kda_chunkwise_workspace_bytes()
- * exceeds 32 MiB (B * H * ceil(T / 64) > 508 on the tensor-core path).  The
+ * exceeds 32 MiB (B * H * ceil(T / 64) > 407 on the tensor-core path).  The
  * first call on a device looks up the array's address (cudaGetSymbolAddress),
  * so make it before any CUDA-graph capture; every GPU that loads the library
  * holds the array until exit.  All calls share the array: calls whose kernels

@@ -9,12 +9,14 @@
 //      L[c,i]    = beta_c sum_k k_ck k_ik exp(gc_ck - gc_ik), i < c  (kda.py:159-165)
 //      Aout[c,i] = sum_k s q_ck k_ik exp(gc_ck - gc_ik),      i <= c (kda.py:166-168)
 //      M = (I + L)^-1 Diag(beta)                             (kda.py:170-171)
-//      W = M (exp(gc) * K)                                   (kda.py:172)
+//      W = M (exp(gc) * K),  U = M V                         (kda.py:172-173)
 //      Qbar = s q exp(gc),  Kbar = exp(gc_last - gc) k,  d = exp(gc_last)
-//    and writes them, with V converted to f16, as ONE 82,432-byte image per
-//    chunk whose byte layout is exactly the tcgen05 shared-memory operand
-//    layout the second kernel uses, so that kernel moves a chunk with two bulk
-//    (TMA-engine) copies: the shared operands and its own slice of V.
+//      E = Qbar - Aout W,   F = Aout U
+//    (kda.py:177-178 give O = Qbar S + Aout (U - W S) = E S + F, so the state
+//    pass needs no Aout product of its own) and writes them as ONE
+//    82,432-byte image per chunk whose byte layout is exactly the shared-memory
+//    layout the second kernel uses, so that kernel moves a chunk with three
+//    bulk (TMA-engine) copies: the shared operands and its slices of U and F.
 //
 //    The decay products exp(gc_c - gc_i) are never formed pair by pair.  The
 //    chunk is split into four 16-row blocks; with the per-step decays
@@ -34,11 +36,11 @@
 //
 // 2. state_kernel -- one CTA per (b, h, slice of VS value columns), walking the
 //    chunks in order with the fp32 state S[128, VS] resident in TMEM.  Per
-//    chunk (kda.py:176-182):
-//      R2 = [M; Aout] V            R1 = [-W; Qbar] S          (tcgen05)
-//      P  = R2[0:64] + R1[0:64]  (= U - W S)                  (registers -> smem f16)
-//      R1 += [M; Aout] P  -> rows 64..127 = Qbar S + Aout P = O  (tcgen05)
-//      R3  = d * S,  R3 += Kbar^T P  -> next S                  (tcgen05)
+//    chunk (kda.py:176-182), 12 tcgen05 MMAs in two dependent batches:
+//      R1  = [-W; E] S                                        (8 MMAs, K = 128)
+//      P   = U + R1[0:64]  (= U - W S)   -> smem f16          (warps 0-1)
+//      O   = R1[64:128] + F  (= Qbar S + Aout P)  -> global   (warps 2-3)
+//      R3  = d * S,  R3 += Kbar^T P  -> next S                (4 MMAs, K = 64)
 //    Operands are f16 (bf16 inputs are exactly representable in f16 at these
 //    magnitudes); every product accumulates in fp32 TMEM, and the carried
 //    state never leaves fp32 (the reference rounds S to the transient dtype
@@ -58,17 +60,19 @@ __device__ int g_kda_device_error = 0;
 namespace tc {
 
 constexpr int CH = 64;        // rows per chunk
-constexpr int KD = 128;       // head dim K of this path
-// chunk image (bytes); all operands f16 in the no-swizzle core-matrix layout
-// (8 rows x 16 bytes per core matrix; LBO = stride along K, SBO = along M/N)
-constexpr int IMG_A1 = 0;         // [-W; Qbar]  128 x 128 K-major, LBO 128, SBO 2048
-constexpr int IMG_A2 = 32768;     // [M; Aout]   128 x 64  K-major, LBO 128, SBO 1024
-constexpr int IMG_A3 = 49152;     // Kbar^T      128 x 64  K-major, LBO 128, SBO 1024
-constexpr int IMG_D = 65536;      // d = exp(gc_last), fp32[128]
-constexpr int IMG_SHARED = 66048; // bytes every value slice needs
-constexpr int IMG_V = 66048;      // V 64 x 128 MN-major, LBO 128, SBO 1024 (slice v0: +v0*128)
+constexpr int KD = 128;       // head dim K (= V) of this path
+// Chunk image (bytes).  A1 and A3 are tcgen05 A operands in the no-swizzle
+// K-major core-matrix layout (8 rows x 16 bytes per core matrix; LBO = stride
+// along K, SBO = along M).  U and F are read by threads; their layout
+// (v/8)*1024 + c*16 + (v%8)*2 keeps a slice of value columns v0..v0+VS one
+// contiguous byte range (v0*128 .. (v0+VS)*128).
+constexpr int IMG_A1 = 0;         // [-W; E]   128 x 128 f16, LBO 128, SBO 2048  (E = Qbar - Aout W)
+constexpr int IMG_A3 = 32768;     // Kbar^T    128 x 64  f16, LBO 128, SBO 1024
+constexpr int IMG_D = 49152;      // d = exp(gc_last), fp32[128]
+constexpr int IMG_SHARED = 49664; // bytes every value slice needs
+constexpr int IMG_U = 49664;      // U = M V        64 x 128 f16
+constexpr int IMG_F = 66048;      // F = Aout U     64 x 128 f16
 constexpr int IMG_BYTES = 82432;
-constexpr int IMG_PAD = 66560;    // shared part rounded up to 1 KiB (stage layout)
 
 constexpr float kSteep = 80.f;                  // block decay beyond which exp(-Z) is unsafe
 constexpr uint64_t kWaitNs = 2000000000ull;     // bound on every mbarrier wait (2 s)
@@ -79,25 +83,33 @@ __device__ __forceinline__ int a1_off(int m, int k) {
 __device__ __forceinline__ int a2_off(int m, int k) {
   return (m >> 3) * 1024 + (k >> 3) * 128 + (m & 7) * 16 + (k & 7) * 2;
 }
-// MN-major B operand with K = 64 rows: offset(c, v)
+// thread-read 64 x 128 layout of V, U and F: offset(c, v)
 __device__ __forceinline__ int vb_off(int c, int v) {
-  return (v >> 3) * 1024 + (c >> 3) * 128 + (c & 7) * 16 + (v & 7) * 2;
+  return (v >> 3) * 1024 + c * 16 + (v & 7) * 2;
 }
 
-// two consecutive innermost elements as fp32 (vector load when `vec`)
-template <typename T>
-__device__ __forceinline__ float2 ld2(const T* p, bool vec) {
-  if (vec) {
-    if constexpr (std::is_same<T, float>::value) return *reinterpret_cast<const float2*>(p);
-    if constexpr (std::is_same<T, __half>::value)
-      return __half22float2(*reinterpret_cast<const __half2*>(p));
-    if constexpr (std::is_same<T, __nv_bfloat16>::value)
-      return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+// two consecutive innermost elements as fp32 through the read-only path
+template <bool VEC, typename T>
+__device__ __forceinline__ float2 ldg2(const T* p) {
+  if constexpr (VEC) {
+    if constexpr (std::is_same<T, float>::value) {
+      return __ldg(reinterpret_cast<const float2*>(p));
+    } else {
+      const unsigned int u = __ldg(reinterpret_cast<const unsigned int*>(p));
+      if constexpr (std::is_same<T, __half>::value)
+        return __half22float2(*reinterpret_cast<const __half2*>(&u));
+      else
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+    }
+  } else {
+    return make_float2(ld(p), ld(p + 1));
   }
-  return make_float2(ld(p), ld(p + 1));
 }
 __device__ __forceinline__ void st_h2(uint8_t* base, int off, float a, float b) {
   *reinterpret_cast<__half2*>(base + off) = __floats2half2_rn(a, b);
+}
+__device__ __forceinline__ float2 ld_h2(const uint8_t* base, int off) {
+  return __half22float2(*reinterpret_cast<const __half2*>(base + off));
 }
 
 // ---------------------------------------------------------------------------
@@ -106,19 +118,22 @@ __device__ __forceinline__ void st_h2(uint8_t* base, int off, float a, float b) 
 constexpr int AXP = 144;   // fp32 pitch of the Gram operands: float4 fragment loads conflict-free
 constexpr int LMP = 68;    // fp32 pitch of L and M
 constexpr int TSP = 24;    // fp32 pitch of the per-warp 16x16 scratch (conflict-free B loads)
-constexpr int P_IMG = 0;
-constexpr int P_AXK = 82944;                           // k * ra          fp32 [64][144]
+constexpr int P_IMG = 0;                               // output image staging
+constexpr int P_A2 = 82944;                            // [M; Aout] f16, K-major LBO 128 SBO 1024
+constexpr int P_AXK = P_A2 + 16384;                    // k * ra          fp32 [64][144]
 constexpr int P_AXQ = P_AXK + CH * AXP * 4;            // s q * ra        fp32 [64][144]
 constexpr int P_YB = P_AXQ + CH * AXP * 4;             // k * nb          fp32 [64][144]
 constexpr int P_LM = P_YB + CH * AXP * 4;              // L               fp32 [64][68]
-constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4],Z[4],a0  [12][128]
-constexpr int P_BETA = P_FAC + 12 * KD * 4;            // beta            fp32 [64]
+constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4]  fp32 [7][128]
+constexpr int P_BETA = P_FAC + 7 * KD * 4;             // beta            fp32 [64]
 constexpr int P_STEEP = P_BETA + CH * 4;               // steep bits      u32 [4][4]
 constexpr int PREP_SMEM = P_STEEP + 16 * 4;
-static_assert(P_AXK >= IMG_BYTES, "image staging");
+static_assert(P_A2 >= IMG_BYTES, "image staging");
 static_assert(PREP_SMEM <= 227 * 1024, "prep shared memory");
-// M (fp32, pitch LMP) reuses the k*ra array once the Gram is done, and the
-// inversion scratch the q*ra array
+// Aliases once their owners are dead: block decays Z[4][128] and exp(g_0)[128]
+// live in the L array during phase 1 (L is written only in phase 2, and only
+// where it is read later); M (fp32, pitch LMP) reuses the k*ra array and the
+// inversion scratch the q*ra array once the Gram is done.
 constexpr int PREP_THREADS = 256;
 
 // 3xTF32 split: x ~= hi + lo with both parts exact in tf32
@@ -133,13 +148,15 @@ __device__ __forceinline__ void mma3_tf32(float* acc, const uint32_t* ah, const 
   ptx::mma_tf32_16x8x8(acc, ah, bh);
 }
 
-// C[16x16] = A[16 x 8*ksteps] * B[8*ksteps x 16] in ~fp32 precision (3xTF32);
-// A(row, k) = Ab[row*lda + k], B(k, col) = Bb[k*ldb + col]; result in acc[2][4]
-// (n-tile nt: rows gid / gid+8, cols 8nt + 2tig (+1))
+// C[16x16] += A[16 x 8*KSTEPS] * B[8*KSTEPS x 16] at ~fp32 accuracy (3xTF32);
+// A(row, k) = Ab[row*lda + k], B(k, col) = Bb[k*ldb + col]; acc[nt] holds
+// rows gid / gid+8, cols 8nt + 2tig (+1)
+template <int KSTEPS>
 __device__ __forceinline__ void gemm16_3xtf32(float (*acc)[4], const float* Ab, int lda,
-                                              const float* Bb, int ldb, int ksteps, int lane) {
+                                              const float* Bb, int ldb, int lane) {
   const int gid = lane >> 2, tig = lane & 3;
-  for (int ks = 0; ks < ksteps; ++ks) {
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
     const int k0 = 8 * ks;
     uint32_t ah[4], al[4];
     split_tf32(Ab[gid * lda + k0 + tig], ah[0], al[0]);
@@ -156,25 +173,50 @@ __device__ __forceinline__ void gemm16_3xtf32(float (*acc)[4], const float* Ab, 
   }
 }
 
-template <typename TIO>
+// acc(16 rows of block rb x 128 columns) = A[rows 16rb.., k < 16(rb+1)] * B, where A
+// is f16 K-major (a2_off geometry, row offset a_row0) and B is either the
+// K-major a1 geometry (k rows, 128 columns) or the vb geometry.
+template <bool B_IS_VB>
+__device__ __forceinline__ void gemm_rowblock_f16(float (*acc)[4], const uint8_t* A, int a_row0,
+                                                  const uint8_t* Bm, int rb, int lane) {
+  const int mi = lane >> 3;
+  for (int ks = 0; ks <= rb; ++ks) {
+    uint32_t a[4];
+    ptx::ldmatrix_x4(a, A + a2_off(a_row0 + 16 * rb + (lane & 7) + ((mi & 1) ? 8 : 0),
+                                   16 * ks + ((mi & 2) ? 8 : 0)));
+#pragma unroll
+    for (int nt = 0; nt < 16; nt += 2) {
+      uint32_t bq[4];
+      const int kr = 16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0);
+      const int kc = 8 * nt + ((mi & 2) ? 8 : 0);
+      ptx::ldmatrix_x4_trans(bq, Bm + (B_IS_VB ? vb_off(kr, kc) : a1_off(kr, kc)));
+      ptx::mma_f16_16x8x16(acc[nt], a, bq);
+      ptx::mma_f16_16x8x16(acc[nt + 1], a, bq + 2);
+    }
+  }
+}
+
+template <typename TIO, bool VEC>
 __global__ void __launch_bounds__(PREP_THREADS, 1)
 prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* img = sm + P_IMG;
+  uint8_t* A2 = sm + P_A2;
   float* Axk = reinterpret_cast<float*>(sm + P_AXK);
   float* Axq = reinterpret_cast<float*>(sm + P_AXQ);
   float* Yb = reinterpret_cast<float*>(sm + P_YB);
   float* Lm = reinterpret_cast<float*>(sm + P_LM);
+  float* Zs = Lm;                  // [4][128] block decays (phase 1 only)
+  float* A0 = Lm + 4 * KD;         // [128]    exp(g of row 0) (phase 1 only)
   float* P02 = reinterpret_cast<float*>(sm + P_FAC);
   float* P03 = P02 + KD;
   float* P13 = P03 + KD;
   float* Ef = P13 + KD;            // [4][128]  exp(-Z_r), 0 for steep channels
-  float* Zs = Ef + 4 * KD;         // [4][128]  block decays Z_r
-  float* A0 = Zs + 4 * KD;         // [128]     exp(g of row 0)
   float* sbeta = reinterpret_cast<float*>(sm + P_BETA);
   uint32_t* steep = reinterpret_cast<uint32_t*>(sm + P_STEEP);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int NT = gridDim.x;
   const int t0 = n * CH;
@@ -186,42 +228,46 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   const float* gb = p.g + b * p.g_s[0] + h * p.g_s[2];
   const float* bb = p.beta + b * p.b_s[0] + h * p.b_s[2];
 
-  // ---- 0. zero L, the Aout half of [M; Aout], the steep mask; beta ---------
-  for (int i = tid; i < CH * LMP; i += PREP_THREADS) Lm[i] = 0.f;
-  for (int i = tid; i < 8192 / 16; i += PREP_THREADS)
-    reinterpret_cast<int4*>(img + IMG_A2 + 8192)[i] = make_int4(0, 0, 0, 0);
   if (tid < 16) steep[tid] = 0u;
   if (tid < CH) sbeta[tid] = (tid < nvalid) ? bb[(int64_t)(t0 + tid) * p.b_s[1]] : 0.f;
 
   // ---- 1. per (16-row block r, channel pair): decays and decayed operands --
   const int r = tid >> 6, k0 = 2 * (tid & 63);
+  // every input row of this thread, loaded unconditionally (rows past T are
+  // clamped to the last valid row and zeroed below) so the loads overlap
+  float2 gr[17], qr[16], kr[16], vr[16];
+#pragma unroll
+  for (int i = 0; i < 17; ++i) {
+    const int c = min(16 * r + i, nvalid - 1);
+    gr[i] = ldg2<VEC>(gb + (int64_t)(t0 + c) * p.g_s[1] + k0);
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = min(16 * r + i, nvalid - 1);
+    qr[i] = ldg2<VEC>(qb + (int64_t)(t0 + c) * p.q_s[1] + k0);
+    kr[i] = ldg2<VEC>(kb + (int64_t)(t0 + c) * p.k_s[1] + k0);
+    vr[i] = ldg2<VEC>(vb + (int64_t)(t0 + c) * p.v_s[1] + k0);
+  }
   float2 al[17];                    // al[i] = exp(g) of row 16r + i (i >= 1)
-  float2 zr;
-  {
-    float2 gr[17];
+  float2 zr = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 17; ++i) {
-      const int c = 16 * r + i;
-      gr[i] = (c < nvalid) ? ld2(gb + (int64_t)(t0 + c) * p.g_s[1] + k0, p.g_vec2)
-                           : make_float2(0.f, 0.f);
-    }
-    // Z_r = sum of g over rows 16r+1 .. 16r+16 (..63 for the last block)
-    zr = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int i = 1; i < 17; ++i) {
-      if (i == 16 && r == 3) break;
+  for (int i = 0; i < 17; ++i) {
+    const bool ok = (16 * r + i < nvalid) && !(i == 16 && r == 3);
+    if (!ok) gr[i] = make_float2(0.f, 0.f);
+    if (i >= 1) {
       zr.x += gr[i].x;
       zr.y += gr[i].y;
+      al[i] = make_float2(__expf(gr[i].x), __expf(gr[i].y));
     }
+  }
 #pragma unroll
-    for (int i = 1; i < 17; ++i) al[i] = make_float2(__expf(gr[i].x), __expf(gr[i].y));
-    if (r == 3) al[16] = make_float2(1.f, 1.f);
-    Zs[r * KD + k0] = zr.x;
-    Zs[r * KD + k0 + 1] = zr.y;
-    if (r == 0) {
-      A0[k0] = expf(gr[0].x);
-      A0[k0 + 1] = expf(gr[0].y);
-    }
+  for (int i = 0; i < 16; ++i)
+    if (16 * r + i >= nvalid) qr[i] = kr[i] = vr[i] = make_float2(0.f, 0.f);
+  Zs[r * KD + k0] = zr.x;
+  Zs[r * KD + k0 + 1] = zr.y;
+  if (r == 0) {
+    A0[k0] = expf(gr[0].x);
+    A0[k0 + 1] = expf(gr[0].y);
   }
   __syncthreads();
   {
@@ -255,6 +301,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     }
     // ra: prefix products from the block start; nb: suffix products to the next block start
     float2 ra[16], nb[16];
+    if (r == 3) al[16] = make_float2(1.f, 1.f);
     ra[0] = make_float2(1.f, 1.f);
 #pragma unroll
     for (int i = 1; i < 16; ++i) ra[i] = make_float2(ra[i - 1].x * al[i].x, ra[i - 1].y * al[i].y);
@@ -262,31 +309,25 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 #pragma unroll
     for (int i = 14; i >= 0; --i)
       nb[i] = make_float2(nb[i + 1].x * al[i + 1].x, nb[i + 1].y * al[i + 1].y);
-    float kbx[16], kby[16];         // Kbar for the transposed store
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int c = 16 * r + i;
-      float2 qv = make_float2(0.f, 0.f), kv = qv, vv = qv;
-      if (c < nvalid) {
-        qv = ld2(qb + (int64_t)(t0 + c) * p.q_s[1] + k0, p.qk_vec2);
-        kv = ld2(kb + (int64_t)(t0 + c) * p.k_s[1] + k0, p.qk_vec2);
-        vv = ld2(vb + (int64_t)(t0 + c) * p.v_s[1] + k0, p.v_vec2);
-      }
+      const float2 qv = qr[i], kv = kr[i], vv = vr[i];
       const float qsx = qv.x * s, qsy = qv.y * s;
       const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;     // exp(gc_c)
-      st_h2(img, IMG_A1 + a1_off(64 + c, k0), qsx * egx, qsy * egy);   // Qbar
-      st_h2(img, IMG_A1 + a1_off(c, k0), kv.x * egx, kv.y * egy);      // Ktilde
-      st_h2(img, IMG_V + vb_off(c, k0), vv.x, vv.y);                   // V (f16)
-      kbx[i] = kv.x * nb[i].x * afx;                                   // Kbar
-      kby[i] = kv.y * nb[i].y * afy;
+      st_h2(img, IMG_A1 + a1_off(64 + c, k0), qsx * egx, qsy * egy);   // Qbar (-> E later)
+      st_h2(img, IMG_A1 + a1_off(c, k0), kv.x * egx, kv.y * egy);      // Ktilde (-> -W later)
+      st_h2(img, IMG_U + vb_off(c, k0), vv.x, vv.y);                   // V (-> U later)
       *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
       *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
       *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
     }
 #pragma unroll
-    for (int i = 0; i < 16; i += 2) {
-      st_h2(img, IMG_A3 + a2_off(k0, 16 * r + i), kbx[i], kbx[i + 1]);
-      st_h2(img, IMG_A3 + a2_off(k0 + 1, 16 * r + i), kby[i], kby[i + 1]);
+    for (int i = 0; i < 16; i += 2) {                               // Kbar^T (k rows, c cols)
+      st_h2(img, IMG_A3 + a2_off(k0, 16 * r + i), kr[i].x * nb[i].x * afx,
+            kr[i + 1].x * nb[i + 1].x * afx);
+      st_h2(img, IMG_A3 + a2_off(k0 + 1, 16 * r + i), kr[i].y * nb[i].y * afy,
+            kr[i + 1].y * nb[i + 1].y * afy);
     }
   }
   __syncthreads();
@@ -295,26 +336,21 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   // The K order inside each 16-channel group is permuted (sums are order-free)
   // so every fragment element pair comes from one float4 load.
   {
-    const int gid = lane >> 2, tig = lane & 3;
     const int rr = warp & 3, type = warp >> 2;          // type 0: L (x = k), 1: Aout (x = s q)
     const float* Ax = type ? Axq : Axk;
     uint32_t af[8][2][4];                               // [16-channel group][k-step][frag]
-    float4 arow0[8], arow1[8];
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
-      arow0[g] = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid) * AXP + 16 * g + 4 * tig);
-      arow1[g] = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid + 8) * AXP + 16 * g + 4 * tig);
-    }
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      af[g][0][0] = ptx::f32_to_tf32(arow0[g].x);
-      af[g][0][1] = ptx::f32_to_tf32(arow1[g].x);
-      af[g][0][2] = ptx::f32_to_tf32(arow0[g].y);
-      af[g][0][3] = ptx::f32_to_tf32(arow1[g].y);
-      af[g][1][0] = ptx::f32_to_tf32(arow0[g].z);
-      af[g][1][1] = ptx::f32_to_tf32(arow1[g].z);
-      af[g][1][2] = ptx::f32_to_tf32(arow0[g].w);
-      af[g][1][3] = ptx::f32_to_tf32(arow1[g].w);
+      const float4 a0 = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid) * AXP + 16 * g + 4 * tig);
+      const float4 a1 = *reinterpret_cast<const float4*>(Ax + (16 * rr + gid + 8) * AXP + 16 * g + 4 * tig);
+      af[g][0][0] = ptx::f32_to_tf32(a0.x);
+      af[g][0][1] = ptx::f32_to_tf32(a1.x);
+      af[g][0][2] = ptx::f32_to_tf32(a0.y);
+      af[g][0][3] = ptx::f32_to_tf32(a1.y);
+      af[g][1][0] = ptx::f32_to_tf32(a0.z);
+      af[g][1][1] = ptx::f32_to_tf32(a1.z);
+      af[g][1][2] = ptx::f32_to_tf32(a0.w);
+      af[g][1][3] = ptx::f32_to_tf32(a1.w);
     }
     for (int j = 0; j <= rr; ++j) {
       const float* f = nullptr;                         // per-channel factor on the B side
@@ -360,12 +396,21 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
                   const float xr = type ? s * ld(qb + (int64_t)(t0 + c) * p.q_s[1] + kk)
                                         : ld(kb + (int64_t)(t0 + c) * p.k_s[1] + kk);
                   const float ki = ld(kb + (int64_t)(t0 + i) * p.k_s[1] + kk);
-                  acc[nt][e] = fmaf(xr * ki, expf(pre[rl] - pre[cl]), acc[nt][e]);
+                  float prl = 0.f, pcl = 0.f;              // static indexing of pre[]
+#pragma unroll
+                  for (int u = 0; u < 16; ++u) {
+                    prl = (u == rl) ? pre[u] : prl;
+                    pcl = (u == cl) ? pre[u] : pcl;
+                  }
+                  acc[nt][e] = fmaf(xr * ki, expf(prl - pcl), acc[nt][e]);
                 }
               }
           }
         }
       }
+      // L (type 0) where the inversion reads it: strictly below the diagonal.
+      // Aout (type 1) as the f16 A operand of phase 5: the full lower blocks
+      // plus zeros above the diagonal inside the diagonal block.
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -375,8 +420,9 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
           const float v = acc[nt][e];
           if (type == 0) {
             if (col < row) Lm[row * LMP + col] = sbeta[row] * v;
-          } else if (col <= row) {
-            *reinterpret_cast<__half*>(img + IMG_A2 + a2_off(64 + row, col)) = __float2half_rn(v);
+          } else {
+            *reinterpret_cast<__half*>(A2 + a2_off(64 + row, col)) =
+                __float2half_rn(col <= row ? v : 0.f);
           }
         }
     }
@@ -390,13 +436,20 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     const int rb = warp;
     if (lane < 16) {
       const int j = lane;
+      // fixed-trip loops with the triangle as a compile-time guard keep x in registers
       float x[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        float acc = (c == j) ? 1.f : 0.f;
+        const float* lrow = Lm + (16 * rb + c) * LMP + 16 * rb;
+        float a0 = (c == j) ? 1.f : 0.f, a1 = 0.f;
 #pragma unroll
-        for (int i = 0; i < c; ++i) acc = fmaf(-Lm[(16 * rb + c) * LMP + 16 * rb + i], x[i], acc);
-        x[c] = acc;
+        for (int i = 0; i < 16; ++i) {
+          if (i < c) {
+            if (i & 1) a1 = fmaf(-lrow[i], x[i], a1);
+            else a0 = fmaf(-lrow[i], x[i], a0);
+          }
+        }
+        x[c] = a0 + a1;
       }
 #pragma unroll
       for (int c = 0; c < 16; ++c) Mm[(16 * rb + c) * LMP + 16 * rb + j] = x[c];
@@ -412,10 +465,12 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   for (int dist = 1; dist <= 3; ++dist) {
     if (warp < 4 - dist) {
       const int j = warp, rb = warp + dist;
-      const int gid = lane >> 2, tig = lane & 3;
       float tacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      gemm16_3xtf32(tacc, Lm + (16 * rb) * LMP + 16 * j, LMP, Mm + (16 * j) * LMP + 16 * j, LMP,
-                    2 * dist, lane);
+      const float* La = Lm + (16 * rb) * LMP + 16 * j;
+      const float* Mb = Mm + (16 * j) * LMP + 16 * j;
+      if (dist == 1) gemm16_3xtf32<2>(tacc, La, LMP, Mb, LMP, lane);
+      else if (dist == 2) gemm16_3xtf32<4>(tacc, La, LMP, Mb, LMP, lane);
+      else gemm16_3xtf32<6>(tacc, La, LMP, Mb, LMP, lane);
       float* T = Ts + warp * (16 * TSP);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
@@ -424,7 +479,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
           T[(gid + 8 * (e >> 1)) * TSP + 8 * nt + 2 * tig + (e & 1)] = tacc[nt][e];
       __syncwarp();
       float macc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      gemm16_3xtf32(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, T, TSP, 2, lane);
+      gemm16_3xtf32<2>(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, T, TSP, lane);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -436,50 +491,71 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   }
   for (int idx = tid; idx < CH * CH / 2; idx += PREP_THREADS) {
     const int row = idx >> 5, col = 2 * (idx & 31);
-    st_h2(img, IMG_A2 + a2_off(row, col), Mm[row * LMP + col] * sbeta[col],
+    st_h2(A2, a2_off(row, col), Mm[row * LMP + col] * sbeta[col],
           Mm[row * LMP + col + 1] * sbeta[col + 1]);
   }
   __syncthreads();
 
-  // ---- 4. W = M Ktilde (f16 mma.sync); store -W over Ktilde ----------------
+  // ---- 4. [W | U] = M [Ktilde | V]; store -W over Ktilde and U over V ------
   {
-    const int gid = lane >> 2, tig = lane & 3;
-    const int rb = warp & 3, ch = warp >> 2;
-    float acc[8][4];
+    const int rb = warp & 3, half = warp >> 2;
+    float acc[16][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+    for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    const int mi = lane >> 3;
-    for (int ks = 0; ks <= rb; ++ks) {
-      uint32_t a[4];
-      ptx::ldmatrix_x4(a, img + IMG_A2 + a2_off(16 * rb + (lane & 7) + ((mi & 1) ? 8 : 0),
-                                                16 * ks + ((mi & 2) ? 8 : 0)));
-#pragma unroll
-      for (int nt = 0; nt < 8; nt += 2) {
-        uint32_t bq[4];
-        ptx::ldmatrix_x4_trans(bq, img + IMG_A1 + a1_off(16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0),
-                                                         64 * ch + 8 * nt + ((mi & 2) ? 8 : 0)));
-        ptx::mma_f16_16x8x16(acc[nt], a, bq);
-        ptx::mma_f16_16x8x16(acc[nt + 1], a, bq + 2);
-      }
-    }
+    if (half == 0) gemm_rowblock_f16<false>(acc, A2, 0, img + IMG_A1, rb, lane);
+    else gemm_rowblock_f16<true>(acc, A2, 0, img + IMG_U, rb, lane);
     __syncthreads();
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+    for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
-        const int row = 16 * rb + gid + 8 * hr;
-        const int col = 64 * ch + 8 * nt + 2 * tig;
-        st_h2(img, IMG_A1 + a1_off(row, col), -acc[nt][2 * hr], -acc[nt][2 * hr + 1]);
+        const int row = 16 * rb + gid + 8 * hr, col = 8 * nt + 2 * tig;
+        if (half == 0)
+          st_h2(img, IMG_A1 + a1_off(row, col), -acc[nt][2 * hr], -acc[nt][2 * hr + 1]);
+        else
+          st_h2(img, IMG_U + vb_off(row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
       }
   }
   __syncthreads();
 
-  // ---- 5. image -> workspace ----------------------------------------------
-  int4* dst = reinterpret_cast<int4*>(ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES);
-  const int4* src = reinterpret_cast<const int4*>(img);
-  for (int i = tid; i < IMG_BYTES / 16; i += PREP_THREADS) dst[i] = src[i];
+  // ---- 5. [E | F] = [Qbar | 0] + Aout [-W | U]; E over Qbar -----------------
+  {
+    const int rb = warp & 3, half = warp >> 2;
+    float acc[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        float2 q0 = make_float2(0.f, 0.f);
+        if (half == 0) q0 = ld_h2(img, IMG_A1 + a1_off(64 + 16 * rb + gid + 8 * hr, 8 * nt + 2 * tig));
+        acc[nt][2 * hr] = q0.x;
+        acc[nt][2 * hr + 1] = q0.y;
+      }
+    if (half == 0) gemm_rowblock_f16<false>(acc, A2, 64, img + IMG_A1, rb, lane);
+    else gemm_rowblock_f16<true>(acc, A2, 64, img + IMG_U, rb, lane);
+    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int row = 16 * rb + gid + 8 * hr, col = 8 * nt + 2 * tig;
+        if (half == 0)
+          st_h2(img, IMG_A1 + a1_off(64 + row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
+        else
+          st_h2(img, IMG_F + vb_off(row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
+      }
+  }
+  ptx::fence_proxy_async_smem();
+  __syncthreads();
+
+  // ---- 6. image -> workspace (bulk store through the TMA engine) -----------
+  if (tid == 0) {
+    ptx::bulk_s2g(ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES, img, IMG_BYTES);
+    ptx::bulk_commit();
+    ptx::bulk_wait_read();
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -488,14 +564,16 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 template <int VS>
 struct StateCfg {
   static constexpr int NCOL = VS <= 16 ? 64 : (VS <= 32 ? 128 : (VS <= 64 ? 256 : 512));
-  static constexpr int R1 = 0, R2 = VS, R3 = 2 * VS;
-  static constexpr int VT_BYTES = CH * VS * 2;                 // V slice, K = 64 rows
-  static constexpr int STAGE = IMG_PAD + ((VT_BYTES + 1023) / 1024) * 1024;
+  static constexpr int R1 = 0, R3 = 2 * VS;                    // TMEM columns
+  static constexpr int SLICE = CH * VS * 2;                    // U or F slice bytes
+  static constexpr int ST_U = 50176;                           // shared part, 1 KiB padded
+  static constexpr int ST_F = ST_U + SLICE;
+  static constexpr int STAGE = ((ST_F + SLICE + 1023) / 1024) * 1024;
   static constexpr int SB_OFF = 2 * STAGE;                     // S  (K = 128) f16
   static constexpr int PB_OFF = SB_OFF + KD * VS * 2;          // P  (K = 64)  f16
   static constexpr int BAR_OFF = PB_OFF + CH * VS * 2;
   static constexpr int SMEM = BAR_OFF + 64;
-  static constexpr uint32_t TX = IMG_SHARED + VT_BYTES;        // bytes per chunk
+  static constexpr uint32_t TX = IMG_SHARED + 2 * SLICE;       // bytes per chunk
   static_assert(SMEM <= 227 * 1024, "state shared memory");
 };
 
@@ -510,6 +588,16 @@ __device__ __forceinline__ int4 pack8_f16(const float* x) {
   r.w = *reinterpret_cast<int*>(&h3);
   return r;
 }
+// 8 f16 (16 bytes) added into 8 fp32
+__device__ __forceinline__ void add8_f16(float* x, int4 v) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    x[2 * i] += f.x;
+    x[2 * i + 1] += f.y;
+  }
+}
 
 __device__ __forceinline__ void named_barrier_64() {
   asm volatile("bar.sync 1, 64;" ::: "memory");
@@ -518,9 +606,11 @@ __device__ __forceinline__ void named_barrier_64() {
 template <int VS>
 __device__ __forceinline__ void fetch_chunk(uint8_t* stg, const uint8_t* img_g, int v0,
                                             uint64_t* bar) {
-  ptx::mbar_arrive_expect_tx(bar, StateCfg<VS>::TX);
+  using Cfg = StateCfg<VS>;
+  ptx::mbar_arrive_expect_tx(bar, Cfg::TX);
   ptx::bulk_g2s(stg, img_g, IMG_SHARED, bar);
-  ptx::bulk_g2s(stg + IMG_PAD, img_g + IMG_V + v0 * 128, StateCfg<VS>::VT_BYTES, bar);
+  ptx::bulk_g2s(stg + Cfg::ST_U, img_g + IMG_U + v0 * 128, Cfg::SLICE, bar);
+  ptx::bulk_g2s(stg + Cfg::ST_F, img_g + IMG_F + v0 * 128, Cfg::SLICE, bar);
 }
 
 template <int VS, typename TIO, typename TSI, typename TSO>
@@ -533,9 +623,10 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   uint8_t* Sb = sm + Cfg::SB_OFF;
   uint8_t* Pb = sm + Cfg::PB_OFF;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [2] chunk images
-  uint64_t* mbarA = full + 2;      // first MMA batch of a chunk done (one phase per chunk)
-  uint64_t* mbarB = full + 3;      // second MMA batch of a chunk done (one phase per chunk)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 4);
+  uint64_t* mbarA = full + 2;      // R1 = [-W; E] S done           (one phase per chunk)
+  uint64_t* mbarB = full + 3;      // R3 += Kbar^T P done           (one phase per chunk)
+  uint64_t* fcons = full + 4;      // warps 2-3 finished reading F  (one phase per chunk)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -554,6 +645,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     ptx::mbar_init(&full[1], 1);
     ptx::mbar_init(mbarA, 1);
     ptx::mbar_init(mbarB, 1);
+    ptx::mbar_init(fcons, 64);
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
@@ -563,9 +655,9 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   const uint32_t tbase = *tslot;
   const uint32_t tlane = tbase + (static_cast<uint32_t>(warp * 32) << 16);
 
-  // thread 0: stages with a bulk copy in flight and the parity of its phase
+  // thread 64 (the copy issuer): stages with a bulk copy in flight and their phase parity
   uint32_t pending = 0, pend_par = 0;
-  if (tid == 0) {
+  if (tid == 64) {
     for (int sg = 0; sg < 2 && sg < NT; ++sg) {
       fetch_chunk<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
       pending |= 1u << sg;
@@ -586,14 +678,22 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   }
   ptx::tmem_wait_st();
 
+  // shared-memory descriptors of every operand, both stages (built once);
+  // they advance by 256 bytes (16 in the >>4 address field) per k-step
+  const uint32_t st0 = ptx::smem_u32(sm), st1 = ptx::smem_u32(sm + Cfg::STAGE);
+  const uint64_t dA1_0 = ptx::sdesc(st0 + IMG_A1, 128, 2048), dA1_1 = ptx::sdesc(st1 + IMG_A1, 128, 2048);
+  const uint64_t dA3_0 = ptx::sdesc(st0 + IMG_A3, 128, 1024), dA3_1 = ptx::sdesc(st1 + IMG_A3, 128, 1024);
+  const uint64_t dSb = ptx::sdesc(ptx::smem_u32(Sb), 128, 2048);
+  const uint64_t dPb = ptx::sdesc(ptx::smem_u32(Pb), 128, 1024);
+
   bool aborted = false;
   for (int n = 0; n < NT; ++n) {
     const int sg = n & 1;
     uint8_t* stg = sm + sg * Cfg::STAGE;
-    uint8_t* vt = stg + IMG_PAD;
+    const uint32_t par = static_cast<uint32_t>(n & 1);
     // every thread waits for image n itself (bounded)
     if (ptx::mbar_wait(&full[sg], (n >> 1) & 1, kWaitNs)) {
-      if (tid == 0) pending &= ~(1u << sg);
+      if (tid == 64) pending &= ~(1u << sg);
     } else {
       *abort_flag = 1;
     }
@@ -620,76 +720,68 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     ptx::tc_fence_before();
     __syncthreads();                                       // Sb and d*S ready
     if (*abort_flag) { aborted = true; break; }
-    if (tid == 0) {
+    if (warp == 0) {                                       // warp-uniform issue, one lane
       ptx::tc_fence_after();
-      const uint32_t a2 = ptx::smem_u32(stg + IMG_A2), a1 = ptx::smem_u32(stg + IMG_A1);
-      const uint32_t vb = ptx::smem_u32(vt), sb = ptx::smem_u32(Sb);
+      const uint64_t dA1 = sg ? dA1_1 : dA1_0;
+      if (ptx::elect_one()) {
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)                       // R2 = [M; Aout] V
-        ptx::mma_f16_ss(tbase + Cfg::R2, ptx::sdesc(a2 + 256 * ks, 128, 1024),
-                        ptx::sdesc(vb + 256 * ks, 128, 1024), IDESC, ks > 0);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)                       // R1 = [-W; Qbar] S
-        ptx::mma_f16_ss(tbase + Cfg::R1, ptx::sdesc(a1 + 256 * ks, 128, 2048),
-                        ptx::sdesc(sb + 256 * ks, 128, 2048), IDESC, ks > 0);
-      ptx::tc_commit(mbarA);
+        for (int ks = 0; ks < 8; ++ks)                     // R1 = [-W; E] S
+          ptx::mma_f16_ss(tbase + Cfg::R1, dA1 + 16 * ks, dSb + 16 * ks, IDESC, ks > 0);
+        ptx::tc_commit(mbarA);
+      }
+      __syncwarp();
     }
-    // Warps 0-1 consume the first MMA batch; warps 2-3 only need the second.
-    // Each batch has its own barrier completing once per chunk, so the phase a
-    // thread waits for has parity n & 1 and can never be lapped: the next
-    // phase of either barrier needs the next chunk's CTA barrier.
-    const uint32_t par = static_cast<uint32_t>(n & 1);
+    // every warp needs the first batch (P rows 0-63, O rows 64-127); the
+    // barriers complete once per chunk, so parity n & 1 can never be lapped
+    if (!ptx::mbar_wait(mbarA, par, kWaitNs)) *abort_flag = 1;
+    ptx::tc_fence_after();
     if (warp < 2) {                                        // P = U - W S, rows c = tid
-      if (!ptx::mbar_wait(mbarA, par, kWaitNs)) *abort_flag = 1;
-      ptx::tc_fence_after();
+      const uint8_t* ub = stg + Cfg::ST_U;
 #pragma unroll 1
       for (int pc = 0; pc < NP; ++pc) {
-        float u[CW], w[CW];
-        ptx::tmem_ld<CW>(tlane + Cfg::R2 + pc * CW, u);
-        ptx::tmem_ld<CW>(tlane + Cfg::R1 + pc * CW, w);
+        float u[CW];
+        ptx::tmem_ld<CW>(tlane + Cfg::R1 + pc * CW, u);
         ptx::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < CW; ++j) u[j] += w[j];
-#pragma unroll
-        for (int g8 = 0; g8 < CW / 8; ++g8)
-          *reinterpret_cast<int4*>(Pb + (pc * (CW / 8) + g8) * 1024 + (tid >> 3) * 128 +
-                                   (tid & 7) * 16) = pack8_f16(u + 8 * g8);
+        for (int g8 = 0; g8 < CW / 8; ++g8) {
+          const int gg = pc * (CW / 8) + g8;
+          add8_f16(u + 8 * g8, *reinterpret_cast<const int4*>(ub + gg * 1024 + tid * 16));
+          *reinterpret_cast<int4*>(Pb + gg * 1024 + (tid >> 3) * 128 + (tid & 7) * 16) =
+              pack8_f16(u + 8 * g8);
+        }
       }
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       named_barrier_64();                                  // P ready (warps 0-1)
-      if (tid == 0) {
+      if (warp == 0) {
         ptx::tc_fence_after();
-        const uint32_t a2 = ptx::smem_u32(stg + IMG_A2), a3 = ptx::smem_u32(stg + IMG_A3);
-        const uint32_t pb = ptx::smem_u32(Pb);
+        const uint64_t dA3 = sg ? dA3_1 : dA3_0;
+        if (ptx::elect_one()) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)                     // R3 += Kbar^T P (next state first)
-          ptx::mma_f16_ss(tbase + Cfg::R3, ptx::sdesc(a3 + 256 * ks, 128, 1024),
-                          ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)                     // R1 += [M; Aout] P
-          ptx::mma_f16_ss(tbase + Cfg::R1, ptx::sdesc(a2 + 256 * ks, 128, 1024),
-                          ptx::sdesc(pb + 256 * ks, 128, 1024), IDESC, 1u);
-        ptx::tc_commit(mbarB);
+          for (int ks = 0; ks < 4; ++ks)                   // R3 += Kbar^T P
+            ptx::mma_f16_ss(tbase + Cfg::R3, dA3 + 16 * ks, dPb + 16 * ks, IDESC, 1u);
+          ptx::tc_commit(mbarB);
+        }
+        __syncwarp();
       }
-    }
-    if (!ptx::mbar_wait(mbarB, par, kWaitNs)) *abort_flag = 1;
-    ptx::tc_fence_after();
-    if (tid == 0 && n + 2 < NT && !*abort_flag) {          // stage free: fetch chunk n+2
-      ptx::fence_proxy_async_smem();
-      fetch_chunk<VS>(stg, wsh + (size_t)(n + 2) * IMG_BYTES, v0, &full[sg]);
-      pending |= 1u << sg;
-      pend_par = (pend_par & ~(1u << sg)) | ((((n + 2) >> 1) & 1u) << sg);
-    }
-    if (warp >= 2) {                                       // O rows c = tid - 64
-      const int t = n * CH + (tid - 64);
+    } else {                                               // O = E S + F, rows c = tid - 64
+      const int c = tid - 64;
+      const int t = n * CH + c;
+      const uint8_t* fb = stg + Cfg::ST_F;
       TIO* dst = static_cast<TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] +
                  h * p.o_s[2] + v0;
-#pragma unroll 1
+      int4 fr[VS / 8];                                     // F row first: frees the stage early
+#pragma unroll
+      for (int gg = 0; gg < VS / 8; ++gg)
+        fr[gg] = *reinterpret_cast<const int4*>(fb + gg * 1024 + c * 16);
+      ptx::mbar_arrive(fcons);                             // F of this stage consumed
+#pragma unroll
       for (int pc = 0; pc < NP; ++pc) {
         float o[CW];
         ptx::tmem_ld<CW>(tlane + Cfg::R1 + pc * CW, o);
         ptx::tmem_wait_ld();
+#pragma unroll
+        for (int g8 = 0; g8 < CW / 8; ++g8) add8_f16(o + 8 * g8, fr[pc * (CW / 8) + g8]);
         if (t < T) {
           if (p.o_vec16) {
 #pragma unroll
@@ -700,6 +792,20 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
             for (int j = 0; j < CW; ++j) st(dst + pc * CW + j, o[j]);
           }
         }
+      }
+    }
+    if (!ptx::mbar_wait(mbarB, par, kWaitNs)) *abort_flag = 1;
+    ptx::tc_fence_after();
+    // thread 64 refills the stage (off the chain that warp 0 runs): after the
+    // second batch the MMAs and warps 0-1 are done with it, after fcons warps 2-3
+    if (tid == 64 && n + 2 < NT && !*abort_flag) {         // stage free: fetch chunk n+2
+      if (ptx::mbar_wait(fcons, par, kWaitNs)) {
+        ptx::fence_proxy_async_smem();
+        fetch_chunk<VS>(stg, wsh + (size_t)(n + 2) * IMG_BYTES, v0, &full[sg]);
+        pending |= 1u << sg;
+        pend_par = (pend_par & ~(1u << sg)) | ((((n + 2) >> 1) & 1u) << sg);
+      } else {
+        *abort_flag = 1;
       }
     }
     ptx::tc_fence_before();
@@ -718,7 +824,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
 #pragma unroll
       for (int j = 0; j < CW; ++j) st(dst + pc * CW + j, srow[j]);
     }
-  } else if (tid == 0) {
+  } else if (tid == 64) {
     atomicExch(&g_kda_device_error, 1);
     // let bulk copies still in flight land before this CTA's smem is released
     for (int sg = 0; sg < 2; ++sg)
@@ -757,10 +863,10 @@ cudaError_t launch_state(const ChunkParams& p, const uint8_t* ws, cudaStream_t s
   return cudaGetLastError();
 }
 
-template <typename TIO, typename TSI, typename TSO>
-cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
-  auto prep = prep_kernel<TIO>;
-  static bool attr_set = false;
+template <typename TIO, bool VEC>
+cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
+  auto prep = prep_kernel<TIO, VEC>;
+  static bool attr_set = false;   // one attribute call per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          PREP_SMEM);
@@ -770,7 +876,13 @@ cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   const int NT = (p.T + CH - 1) / CH;
   dim3 pgrid(NT, p.H, p.B);
   prep<<<pgrid, PREP_THREADS, PREP_SMEM, s>>>(p, ws);
-  cudaError_t e = cudaGetLastError();
+  return cudaGetLastError();
+}
+
+template <typename TIO, typename TSI, typename TSO>
+cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
+  const bool vec = p.g_vec2 && p.qk_vec2 && p.v_vec2;
+  cudaError_t e = vec ? launch_prep<TIO, true>(p, ws, s) : launch_prep<TIO, false>(p, ws, s);
   if (e != cudaSuccess) return e;
   switch (pick_vs(p)) {
     case 16: return launch_state<TIO, TSI, TSO, 16>(p, ws, s);

@@ -19,10 +19,12 @@
 
 namespace kda {
 
-template <int CT, int R, typename TIO, typename TSI, typename TSO>
-__global__ void __launch_bounds__(128)
+// FULL: the launch guarantees K == RG * R, V % VT == 0, a state_in, and
+// 16-byte-aligned state rows in and out, so every row / column guard and the
+// scalar fallbacks drop out (the configuration of every model head, K = V = 128).
+template <int NTH, int CT, int R, bool FULL, typename TIO, typename TSI, typename TSO>
+__global__ void __launch_bounds__(NTH, FULL ? 1024 / NTH : 1)
 recurrent_kernel(const RecParams p) {
-  constexpr int NTH = 128;
   constexpr int RG = NTH / CT;   // row groups
   constexpr int VT = 4 * CT;     // columns per CTA
   constexpr int NW = NTH / 32;
@@ -52,10 +54,10 @@ recurrent_kernel(const RecParams p) {
     const int i = rg + RG * r;
 #pragma unroll
     for (int c = 0; c < 4; ++c) S[r][c] = 0.f;
-    if (p.state_in != nullptr && i < K) {
+    if (FULL || (p.state_in != nullptr && i < K)) {
       const TSI* src = static_cast<const TSI*>(p.state_in) + b * p.si_s[0] + h * p.si_s[1] +
                        (int64_t)i * p.si_s[2];
-      if (vec_s && col0 + 3 < V) {
+      if (FULL || (vec_s && col0 + 3 < V)) {
         ld4(src + col0, S[r]);
       } else {
 #pragma unroll
@@ -84,7 +86,7 @@ recurrent_kernel(const RecParams p) {
     float vv[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      vv[c] = (col0 + c < V) ? ld(vb + (int64_t)t * p.v_s[1] + col0 + c) : 0.f;
+      vv[c] = (FULL || col0 + c < V) ? ld(vb + (int64_t)t * p.v_s[1] + col0 + c) : 0.f;
     __syncthreads();
 
     // ---- stage 2: decay and the two projections over my rows ---------------
@@ -92,7 +94,7 @@ recurrent_kernel(const RecParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int i = rg + RG * r;
-      if (i < K) {
+      if (FULL || i < K) {
         const float al = sa[buf][i], kk = sk[buf][i], qq = sq[buf][i];
         qk = fmaf(qq, kk, qk);
 #pragma unroll
@@ -144,7 +146,7 @@ recurrent_kernel(const RecParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int i = rg + RG * r;
-      if (i < K) {
+      if (FULL || i < K) {
         const float kk = sk[buf][i];
 #pragma unroll
         for (int c = 0; c < 4; ++c) S[r][c] = fmaf(kk, u[c], S[r][c]);
@@ -152,7 +154,7 @@ recurrent_kernel(const RecParams p) {
     }
     if (rg == 0) {
       TIO* dst = ob + (int64_t)t * p.o_s[1];
-      if (p.o_vec && col0 + 3 < V) {
+      if (p.o_vec && (FULL || col0 + 3 < V)) {
         st4(dst + col0, o);
       } else {
 #pragma unroll
@@ -166,10 +168,10 @@ recurrent_kernel(const RecParams p) {
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int i = rg + RG * r;
-    if (i < K) {
+    if (FULL || i < K) {
       TSO* dst = static_cast<TSO*>(p.state_out) + b * p.so_s[0] + h * p.so_s[1] +
                  (int64_t)i * p.so_s[2];
-      if (p.state_out_vec && col0 + 3 < V) {
+      if (FULL || (p.state_out_vec && col0 + 3 < V)) {
         st4(dst + col0, S[r]);
       } else {
 #pragma unroll
@@ -183,21 +185,32 @@ recurrent_kernel(const RecParams p) {
 // ---------------------------------------------------------------------------
 // dispatch
 // ---------------------------------------------------------------------------
-template <int CT, int R, typename TIO, typename TSI, typename TSO>
+template <int NTH, int CT, int R, bool FULL, typename TIO, typename TSI, typename TSO>
 static cudaError_t launch_rec(const RecParams& p, cudaStream_t s) {
   constexpr int VT = 4 * CT;
   dim3 grid((p.V + VT - 1) / VT, p.H, p.B);
-  recurrent_kernel<CT, R, TIO, TSI, TSO><<<grid, 128, 0, s>>>(p);
+  recurrent_kernel<NTH, CT, R, FULL, TIO, TSI, TSO><<<grid, NTH, 0, s>>>(p);
   return cudaGetLastError();
 }
 
+#ifndef KDA_REC_FULL_NTH
+#define KDA_REC_FULL_NTH 256
+#endif
+
 template <typename TIO, typename TSI, typename TSO>
 static cudaError_t launch_rec_k(const RecParams& p, cudaStream_t s) {
+  // K = 128 with whole 64-column tiles and vector-aligned states: the guard-free
+  // kernel; NTH / 16 row groups of R rows cover the 128 rows exactly.
+  if (p.K == 128 && p.V % 64 == 0 && p.state_in != nullptr && p.state_vec &&
+      p.state_out_vec) {
+    constexpr int NTH = KDA_REC_FULL_NTH;
+    return launch_rec<NTH, 16, 128 * 16 / NTH, true, TIO, TSI, TSO>(p, s);
+  }
   // (CT, R): RG = 128 / CT row groups of R rows cover K <= RG * R.
-  if (p.K <= 32) return launch_rec<8, 2, TIO, TSI, TSO>(p, s);
-  if (p.K <= 64) return launch_rec<16, 8, TIO, TSI, TSO>(p, s);
-  if (p.K <= 128) return launch_rec<16, 16, TIO, TSI, TSO>(p, s);
-  return launch_rec<16, 32, TIO, TSI, TSO>(p, s);
+  if (p.K <= 32) return launch_rec<128, 8, 2, false, TIO, TSI, TSO>(p, s);
+  if (p.K <= 64) return launch_rec<128, 16, 8, false, TIO, TSI, TSO>(p, s);
+  if (p.K <= 128) return launch_rec<128, 16, 16, false, TIO, TSI, TSO>(p, s);
+  return launch_rec<128, 16, 32, false, TIO, TSI, TSO>(p, s);
 }
 
 template <typename TIO, typename TSI>

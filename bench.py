@@ -17,8 +17,13 @@ Reported, all on the device with CUDA events on the launching stream:
 * ``e2e``       the same metric through the public API from pinned host
                 buffers: H2D of q/k/v/g/beta and D2H of o and S inside the
                 timed region;
-* ``decode``    BASELINE configs[2]: B=64 recurrent single-token steps on a
-                fp32 [64,16,128,128] state, against HBM bandwidth;
+* ``decode``    BASELINE configs[2]: B=64 recurrent single-token step on a
+                fp32 [64,16,128,128] state, captured in a CUDA graph and
+                replayed, against HBM bandwidth;
+* ``long_context`` BASELINE configs[3]: B=8, T=32768 bf16 prefill with a
+                fp32 S0, (b, h) sharded over the ranks (strong scaling), with
+                and without the final gather of o and S to rank 0;
+* ``clocks``    nvidia-smi samples taken inside the timed regions;
 * ``cpu_baseline`` the CPU oracle (oracle/kda_oracle.py, a numpy port of the
                 reference) on a bounded sample, rank 0 at N=1.
 
@@ -74,41 +79,76 @@ def _traffic(kernel, workload):
 # clocks sampled during the timed region
 # --------------------------------------------------------------------------- #
 class ClockSampler:
+    """``nvidia-smi -lms`` in the background for the whole GPU part of the run.
+
+    Samples are kept with their host arrival time; :meth:`mark` brackets each
+    timed region and :meth:`summary` reports only samples inside one.  The
+    sampler waits for nvidia-smi's first line before returning from
+    ``__enter__`` so the short timed regions are covered from their start.
+    """
+
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 20
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
+        self.rows = []
+        self.windows = []
+        self._t0 = None
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.perf_counter(), line))
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.PERIOD_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        threading.Thread(target=self._reader, daemon=True).start()
+        t_end = time.perf_counter() + 10.0
+        while not self.rows and time.perf_counter() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
         return self
 
+    def start(self):
+        self._t0 = time.perf_counter()
+
+    def stop(self):
+        if self._t0 is not None:
+            # a sample reports the period that ends at its arrival
+            self.windows.append((self._t0, time.perf_counter() + self.PERIOD_MS * 1e-3))
+            self._t0 = None
+
     def __exit__(self, *exc):
-        self.out = ""
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
+                self.proc.wait()
 
     def summary(self):
-        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.strip()]
-        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        rows = []
+        for t, line in self.rows:
+            if any(a <= t <= b for a, b in self.windows):
+                r = [c.strip() for c in line.split(",")]
+                if len(r) >= 9:
+                    rows.append(r)
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        num = lambda x: x.replace(".", "", 1).isdigit()  # noqa: E731
+        sm = [float(r[1]) for r in rows if num(r[1])]
+        mx = [float(r[2]) for r in rows if num(r[2])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
@@ -182,23 +222,28 @@ def cpu_port_throughput(t_sample, heads, steps=1, warmup=0):
 # --------------------------------------------------------------------------- #
 # GPU legs
 # --------------------------------------------------------------------------- #
-def _events_time(torch, fn, steps, warmup, flush):
-    """Mean device ms of ``fn`` over ``steps`` runs, L2 flushed before each."""
+def _events_time(torch, fn, steps, warmup, flush, clk=None):
+    """Mean device ms of ``fn`` over ``steps`` runs, L2 flushed before each
+    (the flush is outside the events)."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if clk is not None:
+        clk.start()
     for i in range(steps):
         flush.zero_()
         starts[i].record()
         fn()
         ends[i].record()
     torch.cuda.synchronize()
+    if clk is not None:
+        clk.stop()
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
 
 
-def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world):
+def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world, clk):
     x = kb.synth.make_config(1, seed=0, device=dev)
     q, k, v, g, beta = (x[n] for n in ("q", "k", "v", "g", "beta"))
     f32 = torch.float32
@@ -214,13 +259,14 @@ def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world):
     torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    with ClockSampler(dev.index) as clk:
-        for i in range(steps):
-            flush.zero_()
-            starts[i].record()
-            step()
-            ends[i].record()
-        torch.cuda.synchronize()
+    clk.start()
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clk.stop()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -246,42 +292,119 @@ def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world):
         S_h.copy_(S, non_blocking=True)
 
     e2e_steps = max(5, steps // 4)
-    e2e_ms = _events_time(torch, e2e_step, e2e_steps, 2, flush)
+    e2e_ms = _events_time(torch, e2e_step, e2e_steps, 3, flush, clk)
     e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     path = kb.chunkwise_path(q, k, v, g, beta, chunk_size=CFG1["C"], state_dtype=f32)
-    return ms_step, e2e_t.item(), h2d, d2h, clk.summary(), path
+    return ms_step, e2e_t.item(), h2d, d2h, path
 
 
-def bench_decode(torch, kb, dev, steps, warmup, flush):
-    """Config 2: single-token recurrent steps on a fp32 [64,16,128,128] state."""
+def bench_decode(torch, kb, dev, steps, warmup, flush, clk):
+    """Config 2: one single-token recurrent step on a fp32 [64,16,128,128]
+    state, captured in a CUDA graph the way ``GraphedDecoder`` captures its
+    step (``graph_decode.py:269-289``: warm-up on a side stream, then
+    ``torch.cuda.graph``); the replay is timed with L2 flushed before each."""
     B, H, K, V = CFG2["B"], CFG2["H"], CFG2["K"], CFG2["V"]
-    gen = torch.Generator(device=dev).manual_seed(2)
-    x = kb.synth.make_inputs(B, steps + warmup, H, K, V, dtype=torch.float16, seed=2,
-                             s0_std=0.02, device=dev, generator=gen)
-    state = [x["S0"]]
-    t = [0]
+    x = kb.synth.make_inputs(B, 1, H, K, V, dtype=torch.float16, seed=2, s0_std=0.02,
+                             device=dev)
+    args = [x[n] for n in ("q", "k", "v", "g", "beta")]
+    s0 = x["S0"]
 
     def step():
-        i = t[0] % (steps + warmup)
-        t[0] += 1
-        o, S = kb.kda_recurrent(*(x[n][:, i:i + 1] for n in ("q", "k", "v", "g", "beta")),
-                                state=state[0], state_dtype=torch.float32)
-        state[0] = S
-        return o
+        return kb.kda_recurrent(*args, state=s0, state_dtype=torch.float32)
 
-    ms = _events_time(torch, step, steps, warmup, flush)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        o, S = step()
+    o_e, S_e = step()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_e) and torch.equal(S, S_e), "graph replay differs from eager"
+    ms = _events_time(torch, graph.replay, steps, warmup, flush, clk)
+    del graph
     return ms
+
+
+def bench_long_context(torch, kb, dev, steps, warmup, flush, dist, world, rank, clk):
+    """Config 3: B=8, T=32768, H=16 bf16 prefill with a fp32 S0, (b, h)
+    sharded over the ranks (strong scaling), then o and S gathered to rank 0.
+
+    Every rank draws the same full inputs from one seed on its own GPU and
+    keeps its slice (input generation is outside the timed region).  Timed on
+    the device: the kernel alone (max over ranks), and kernel + gather."""
+    c = kb.synth.CONFIGS[3]
+    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    shard = kb.sharding.plan(B, H, world, rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    # generate per batch row to bound the fp32 transients, keep the local slice
+    parts = {n: [] for n in ("q", "k", "v", "g", "beta", "S0")}
+    for b in range(B):
+        xb = kb.synth.make_inputs(1, T, H, K, V, dtype=c["dtype"], s0_std=c["s0_std"],
+                                  device=dev, generator=gen)
+        for n in parts:
+            parts[n].append(xb[n])
+        del xb
+    full = {n: torch.cat(v) for n, v in parts.items()}
+    del parts
+    loc = {n: kb.sharding.take(full[n], shard, "state" if n == "S0" else "seq").contiguous()
+           for n in full}
+    del full
+    torch.cuda.empty_cache()
+
+    def step():
+        return kb.kda_chunkwise(loc["q"], loc["k"], loc["v"], loc["g"], loc["beta"],
+                                initial_state=loc["S0"], chunk_size=c["C"],
+                                state_dtype=torch.float32)
+
+    ms = _events_time(torch, step, steps, warmup, flush, clk)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = ms_t.item()
+
+    def step_gather():
+        o, S = step()
+        kb.sharding.gather(o, (B, T, H, V), shard, "seq", dst=0)
+        kb.sharding.gather(S, (B, H, K, V), shard, "state", dst=0)
+
+    g_steps = max(2, steps // 2)
+    if dist is not None:
+        dist.barrier()
+    ms_g = _events_time(torch, step_gather, g_steps, 1, flush, clk)
+    ms_g_t = torch.tensor([ms_g], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(ms_g_t, op=dist.ReduceOp.MAX)
+    tokens = B * T
+    th = tokens * H
+    byts = th * (3 * K * 2 + K * 4 + 4 + V * 2) + 2 * B * H * K * V * 4
+    return {"workload": "kda_chunkwise prefill, BASELINE configs[3], (b,h) sharded, "
+                        "o and S gathered to rank 0",
+            "B": B, "T": T, "H": H, "K": K, "V": V, "dtype": "bf16", "s0": "N(0,0.02) fp32",
+            "scaling": "strong", "shard": f"{shard.dim} x{shard.size} per rank",
+            "value": tokens / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "with_gather": {"value": tokens / (ms_g_t.item() * 1e-3), "unit": "tokens/s",
+                            "ms_per_step": ms_g_t.item()},
+            "roofline": {"bound": "hbm", "achieved": byts / world / (ms * 1e-3) / 1e9,
+                         "unit": "GB/s", "algorithmic_bytes": byts}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("kda", "reference"), default="kda")
-    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--decode-steps", type=int, default=1024)
+    ap.add_argument("--long-steps", type=int, default=4,
+                    help="timed steps of the configs[3] leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
     if a.warmup < 3:
@@ -328,13 +451,21 @@ def main():
         dist = td
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    ms_step, e2e_ms, h2d, d2h, clocks, path = bench_prefill(
-        torch, kb, dev, a.steps, a.warmup, flush, dist, world)
-    dec_ms = bench_decode(torch, kb, dev, a.decode_steps, a.warmup, flush)
-    dec_t = torch.tensor([dec_ms], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(dec_t, op=dist.ReduceOp.MAX)
-    dec_ms = dec_t.item()
+    with ClockSampler(dev.index) as clk:
+        ms_step, e2e_ms, h2d, d2h, path = bench_prefill(
+            torch, kb, dev, a.steps, a.warmup, flush, dist, world, clk)
+        dec_ms = bench_decode(torch, kb, dev, a.decode_steps, a.warmup, flush, clk)
+        dec_t = torch.tensor([dec_ms], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(dec_t, op=dist.ReduceOp.MAX)
+        dec_ms = dec_t.item()
+        long_ctx = None
+        if a.long_steps > 0:
+            long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, flush, dist, world,
+                                          rank, clk)
+    clocks = clk.summary()
+    # kernels per prefill call: prep + state pass on the tensor-core path
+    launches_per_call = 2 if path == "tcgen05" else 1
 
     hbm, tc, peak_kind = _peaks()
     tokens = CFG1["B"] * CFG1["T"]
@@ -380,12 +511,14 @@ def main():
             "decode": {"workload": "kda_recurrent single-token step, BASELINE configs[2]",
                        "value": world * CFG2["B"] / (dec_ms * 1e-3), "unit": "tokens/s",
                        "ms_per_step": dec_ms, "steps": a.decode_steps,
+                       "timing": "CUDA-graph replay of one step, L2 flushed before each",
                        "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms * 1e-3) / 1e9,
                                     "peak": hbm, "unit": "GB/s",
                                     "frac": dec_bytes / (dec_ms * 1e-3) / 1e9 / hbm,
                                     "traffic": _traffic("kda_recurrent", "cfg2"),
                                     "algorithmic_bytes": dec_bytes}},
-            "gpu_launches": a.steps,
+            "long_context": long_ctx,
+            "gpu_launches": a.steps * launches_per_call,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

@@ -83,9 +83,34 @@ __device__ __forceinline__ int a1_off(int m, int k) {
 __device__ __forceinline__ int a2_off(int m, int k) {
   return (m >> 3) * 1024 + (k >> 3) * 128 + (m & 7) * 16 + (k & 7) * 2;
 }
-// thread-read 64 x 128 layout of V, U and F: offset(c, v)
+// thread-read 64 x 128 layout of V, U and F: offset(c, v).  Each block of 8
+// value columns is 1 KiB (64 rows x 16 bytes); the row slot is XOR-swizzled
+// with the block index so that writers holding one row of many blocks and
+// readers holding many rows of one block both hit distinct banks.
 __device__ __forceinline__ int vb_off(int c, int v) {
-  return (v >> 3) * 1024 + c * 16 + (v & 7) * 2;
+  return (v >> 3) * 1024 + ((c ^ ((v >> 3) & 7)) << 4) + (v & 7) * 2;
+}
+// pack two fp32 as f16x2
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// 4x4 transpose of 32-bit values across the four lanes of a quad:
+// in: x[i] = value of this lane for item i; out: x[i] = value of lane i for
+// item (lane & 3)
+__device__ __forceinline__ void quad_transpose(uint32_t (&x)[4], int tig) {
+  {
+    const bool hi = tig & 2;
+    const uint32_t r0 = __shfl_xor_sync(0xffffffffu, hi ? x[0] : x[2], 2);
+    const uint32_t r1 = __shfl_xor_sync(0xffffffffu, hi ? x[1] : x[3], 2);
+    if (hi) { x[0] = r0; x[1] = r1; } else { x[2] = r0; x[3] = r1; }
+  }
+  {
+    const bool od = tig & 1;
+    const uint32_t r0 = __shfl_xor_sync(0xffffffffu, od ? x[0] : x[1], 1);
+    const uint32_t r1 = __shfl_xor_sync(0xffffffffu, od ? x[2] : x[3], 1);
+    if (od) { x[0] = r0; x[2] = r1; } else { x[1] = r0; x[3] = r1; }
+  }
 }
 
 // two consecutive innermost elements as fp32 through the read-only path
@@ -196,9 +221,13 @@ __device__ __forceinline__ void gemm_rowblock_f16(float (*acc)[4], const uint8_t
   }
 }
 
-template <typename TIO, bool VEC>
+// LOAD: how phase 1 reads its inputs -- 0 scalar loads, 1 two-element vector
+// loads, 2 vector loads and, every input row being a 16-byte-aligned range,
+// the next wave's L2 prefetch issued as one bulk (TMA-engine) prefetch per row.
+template <typename TIO, int LOAD>
 __global__ void __launch_bounds__(PREP_THREADS, 1)
 prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
+  constexpr bool VEC = LOAD >= 1;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* img = sm + P_IMG;
   uint8_t* A2 = sm + P_A2;
@@ -230,23 +259,70 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 
   if (tid < 16) steep[tid] = 0u;
   if (tid < CH) sbeta[tid] = (tid < nvalid) ? bb[(int64_t)(t0 + tid) * p.b_s[1]] : 0.f;
+  uint8_t* img_g = ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES;
+
+  // L2 prefetch of the inputs of the chunk one SM-count further in launch
+  // order: with one CTA per SM that is about the CTA that starts on this SM
+  // when this one retires, so its loads hit L2 instead of HBM.
+  {
+    const long total = (long)NT * p.H * p.B;
+    const long tgt = n + (long)NT * (h + (long)p.H * b) + ptx::num_sms();
+    if (tgt < total) {
+      const int n2 = (int)(tgt % NT), h2 = (int)((tgt / NT) % p.H), b2 = (int)(tgt / ((long)NT * p.H));
+      if constexpr (LOAD == 2) {                   // one TMA-engine prefetch per row
+        const int c = tid >> 2, part = tid & 3;
+        const int64_t t = (int64_t)n2 * CH + c;
+        if (t < p.T) {
+          if (part == 0)
+            ptx::bulk_prefetch_l2(static_cast<const TIO*>(p.q) + b2 * p.q_s[0] + t * p.q_s[1] + h2 * p.q_s[2], KD * sizeof(TIO));
+          else if (part == 1)
+            ptx::bulk_prefetch_l2(static_cast<const TIO*>(p.k) + b2 * p.k_s[0] + t * p.k_s[1] + h2 * p.k_s[2], KD * sizeof(TIO));
+          else if (part == 2)
+            ptx::bulk_prefetch_l2(static_cast<const TIO*>(p.v) + b2 * p.v_s[0] + t * p.v_s[1] + h2 * p.v_s[2], KD * sizeof(TIO));
+          else
+            ptx::bulk_prefetch_l2(p.g + b2 * p.g_s[0] + t * p.g_s[1] + h2 * p.g_s[2], KD * 4);
+        }
+      } else
+      for (int idx = tid; idx < CH * 10; idx += PREP_THREADS) {
+        const int c = idx / 10, part = idx - 10 * (idx / 10);
+        const int t = n2 * CH + c;
+        if (t >= p.T) continue;
+        const uint8_t* a;
+        if (part < 2)
+          a = reinterpret_cast<const uint8_t*>(static_cast<const TIO*>(p.q) + b2 * p.q_s[0] +
+                                               (int64_t)t * p.q_s[1] + h2 * p.q_s[2]) + 128 * part;
+        else if (part < 4)
+          a = reinterpret_cast<const uint8_t*>(static_cast<const TIO*>(p.k) + b2 * p.k_s[0] +
+                                               (int64_t)t * p.k_s[1] + h2 * p.k_s[2]) + 128 * (part - 2);
+        else if (part < 6)
+          a = reinterpret_cast<const uint8_t*>(static_cast<const TIO*>(p.v) + b2 * p.v_s[0] +
+                                               (int64_t)t * p.v_s[1] + h2 * p.v_s[2]) + 128 * (part - 4);
+        else
+          a = reinterpret_cast<const uint8_t*>(p.g + b2 * p.g_s[0] + (int64_t)t * p.g_s[1] +
+                                               h2 * p.g_s[2]) + 128 * (part - 6);
+        ptx::prefetch_l2(a);
+      }
+    }
+  }
 
   // ---- 1. per (16-row block r, channel pair): decays and decayed operands --
   const int r = tid >> 6, k0 = 2 * (tid & 63);
   // every input row of this thread, loaded unconditionally (rows past T are
   // clamped to the last valid row and zeroed below) so the loads overlap
   float2 gr[17], qr[16], kr[16], vr[16];
+  {
 #pragma unroll
-  for (int i = 0; i < 17; ++i) {
-    const int c = min(16 * r + i, nvalid - 1);
-    gr[i] = ldg2<VEC>(gb + (int64_t)(t0 + c) * p.g_s[1] + k0);
-  }
+    for (int i = 0; i < 17; ++i) {
+      const int c = min(16 * r + i, nvalid - 1);
+      gr[i] = ldg2<VEC>(gb + (int64_t)(t0 + c) * p.g_s[1] + k0);
+    }
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int c = min(16 * r + i, nvalid - 1);
-    qr[i] = ldg2<VEC>(qb + (int64_t)(t0 + c) * p.q_s[1] + k0);
-    kr[i] = ldg2<VEC>(kb + (int64_t)(t0 + c) * p.k_s[1] + k0);
-    vr[i] = ldg2<VEC>(vb + (int64_t)(t0 + c) * p.v_s[1] + k0);
+    for (int i = 0; i < 16; ++i) {
+      const int c = min(16 * r + i, nvalid - 1);
+      qr[i] = ldg2<VEC>(qb + (int64_t)(t0 + c) * p.q_s[1] + k0);
+      kr[i] = ldg2<VEC>(kb + (int64_t)(t0 + c) * p.k_s[1] + k0);
+      vr[i] = ldg2<VEC>(vb + (int64_t)(t0 + c) * p.v_s[1] + k0);
+    }
   }
   float2 al[17];                    // al[i] = exp(g) of row 16r + i (i >= 1)
   float2 zr = make_float2(0.f, 0.f);
@@ -309,35 +385,64 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 #pragma unroll
     for (int i = 14; i >= 0; --i)
       nb[i] = make_float2(nb[i + 1].x * al[i + 1].x, nb[i + 1].y * al[i + 1].y);
+    // Qbar and Ktilde go out as 16-byte core-matrix rows: the four lanes of a
+    // quad hold the four channel pairs of one 8-channel group, so after a quad
+    // transpose of four rows each lane owns one whole row of the group.
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int c = 16 * r + i;
-      const float2 qv = qr[i], kv = kr[i], vv = vr[i];
-      const float qsx = qv.x * s, qsy = qv.y * s;
-      const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;     // exp(gc_c)
-      st_h2(img, IMG_A1 + a1_off(64 + c, k0), qsx * egx, qsy * egy);   // Qbar (-> E later)
-      st_h2(img, IMG_A1 + a1_off(c, k0), kv.x * egx, kv.y * egy);      // Ktilde (-> -W later)
-      st_h2(img, IMG_U + vb_off(c, k0), vv.x, vv.y);                   // V (-> U later)
-      *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
-      *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
-      *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
+    for (int i4 = 0; i4 < 16; i4 += 4) {
+      uint32_t qh[4], kh[4];
+#pragma unroll
+      for (int ii = 0; ii < 4; ++ii) {
+        const int i = i4 + ii, c = 16 * r + i;
+        const float2 qv = qr[i], kv = kr[i], vv = vr[i];
+        const float qsx = qv.x * s, qsy = qv.y * s;
+        const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;   // exp(gc_c)
+        qh[ii] = pack_h2(qsx * egx, qsy * egy);                  // Qbar (-> E later)
+        kh[ii] = pack_h2(kv.x * egx, kv.y * egy);                // Ktilde (-> -W later)
+        st_h2(img, IMG_U + vb_off(c, k0), vv.x, vv.y);           // V (-> U later)
+        *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
+        *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
+        *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
+      }
+      quad_transpose(qh, tig);
+      quad_transpose(kh, tig);
+      const int c = 16 * r + i4 + tig;
+      *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(64 + c, k0 & ~7)) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
+      *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(c, k0 & ~7)) = make_uint4(kh[0], kh[1], kh[2], kh[3]);
     }
+    // Kbar^T (k rows, c cols): eight consecutive c of one channel per 16 bytes
 #pragma unroll
-    for (int i = 0; i < 16; i += 2) {                               // Kbar^T (k rows, c cols)
-      st_h2(img, IMG_A3 + a2_off(k0, 16 * r + i), kr[i].x * nb[i].x * afx,
-            kr[i + 1].x * nb[i + 1].x * afx);
-      st_h2(img, IMG_A3 + a2_off(k0 + 1, 16 * r + i), kr[i].y * nb[i].y * afy,
-            kr[i + 1].y * nb[i + 1].y * afy);
+    for (int i8 = 0; i8 < 16; i8 += 8) {
+      uint32_t ex[4], ey[4];
+#pragma unroll
+      for (int ii = 0; ii < 8; ii += 2) {
+        const int i = i8 + ii;
+        ex[ii / 2] = pack_h2(kr[i].x * nb[i].x * afx, kr[i + 1].x * nb[i + 1].x * afx);
+        ey[ii / 2] = pack_h2(kr[i].y * nb[i].y * afy, kr[i + 1].y * nb[i + 1].y * afy);
+      }
+      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0, 16 * r + i8)) = make_uint4(ex[0], ex[1], ex[2], ex[3]);
+      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0 + 1, 16 * r + i8)) = make_uint4(ey[0], ey[1], ey[2], ey[3]);
     }
   }
+  ptx::fence_proxy_async_smem();
   __syncthreads();
+  if (tid == 0) {              // Kbar^T and d are final: [IMG_A3, IMG_SHARED) leaves now
+    ptx::bulk_s2g(img_g + IMG_A3, img + IMG_A3, IMG_SHARED - IMG_A3);
+    ptx::bulk_commit();
+  }
 
-  // ---- 2. Gram blocks: warp = (row block rr, type); A fragments in registers.
+  // ---- 2. Gram blocks: warp = (row block rr0, type); A fragments in registers.
   // The K order inside each 16-channel group is permuted (sums are order-free)
-  // so every fragment element pair comes from one float4 load.
+  // so every fragment element pair comes from one float4 load.  The 10 block
+  // pairs of a type are spread 2/2/3/3 over its four warps: row block 3 does
+  // j = 0..2 and the row-block-0 warp also takes block (3, 3).
   {
-    const int rr = warp & 3, type = warp >> 2;          // type 0: L (x = k), 1: Aout (x = s q)
+    const int rr0 = warp & 3, type = warp >> 2;         // type 0: L (x = k), 1: Aout (x = s q)
     const float* Ax = type ? Axq : Axk;
+#pragma unroll 1
+    for (int seg = 0; seg < (rr0 == 0 ? 2 : 1); ++seg) {
+    const int rr = seg ? 3 : rr0;
+    const int jlo = seg ? 3 : 0, jhi = seg ? 3 : (rr0 == 3 ? 2 : rr0);
     uint32_t af[8][2][4];                               // [16-channel group][k-step][frag]
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
@@ -352,12 +457,15 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       af[g][1][2] = ptx::f32_to_tf32(a0.w);
       af[g][1][3] = ptx::f32_to_tf32(a1.w);
     }
-    for (int j = 0; j <= rr; ++j) {
+#pragma unroll 1
+    for (int j = jlo; j <= jhi; ++j) {
       const float* f = nullptr;                         // per-channel factor on the B side
       if (j == rr) f = Ef + rr * KD;
       else if (rr - j == 2) f = (j == 0) ? P02 : P13;
       else if (rr - j == 3) f = P03;
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // two partial sums per n-tile (even / odd channel groups): four
+      // independent MMA chains instead of two
+      float acc2[2][2][4] = {};
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
         const int kc = 16 * g + 4 * tig;
@@ -367,10 +475,15 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
           const float4 y = *reinterpret_cast<const float4*>(Yb + (16 * j + 8 * nt + gid) * AXP + kc);
           const uint32_t b0[2] = {ptx::f32_to_tf32(y.x * fv.x), ptx::f32_to_tf32(y.y * fv.y)};
           const uint32_t b1[2] = {ptx::f32_to_tf32(y.z * fv.z), ptx::f32_to_tf32(y.w * fv.w)};
-          ptx::mma_tf32_16x8x8(acc[nt], af[g][0], b0);
-          ptx::mma_tf32_16x8x8(acc[nt], af[g][1], b1);
+          ptx::mma_tf32_16x8x8(acc2[g & 1][nt], af[g][0], b0);
+          ptx::mma_tf32_16x8x8(acc2[g & 1][nt], af[g][1], b1);
         }
       }
+      float acc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[0][nt][e] + acc2[1][nt][e];
       if (j == rr) {
         // exact pair terms of the steep channels of this diagonal block (rare)
 #pragma unroll 1
@@ -426,6 +539,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
           }
         }
     }
+    }
   }
   __syncthreads();
 
@@ -435,22 +549,17 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   if (warp < 4) {                      // diagonal blocks by substitution (fp32)
     const int rb = warp;
     if (lane < 16) {
+      // column j of (I + L_rb)^-1, right-looking: once x[i] is final it is
+      // eliminated from every later row, so each step is one dependent FMA
       const int j = lane;
-      // fixed-trip loops with the triangle as a compile-time guard keep x in registers
+      const float* lb = Lm + (16 * rb) * LMP + 16 * rb;
       float x[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float* lrow = Lm + (16 * rb + c) * LMP + 16 * rb;
-        float a0 = (c == j) ? 1.f : 0.f, a1 = 0.f;
+      for (int c = 0; c < 16; ++c) x[c] = (c == j) ? 1.f : 0.f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          if (i < c) {
-            if (i & 1) a1 = fmaf(-lrow[i], x[i], a1);
-            else a0 = fmaf(-lrow[i], x[i], a0);
-          }
-        }
-        x[c] = a0 + a1;
-      }
+      for (int i = 0; i < 15; ++i)
+#pragma unroll
+        for (int c = i + 1; c < 16; ++c) x[c] = fmaf(-lb[c * LMP + i], x[i], x[c]);
 #pragma unroll
       for (int c = 0; c < 16; ++c) Mm[(16 * rb + c) * LMP + 16 * rb + j] = x[c];
     }
@@ -518,7 +627,13 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
           st_h2(img, IMG_U + vb_off(row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
       }
   }
+  ptx::fence_proxy_async_smem();
   __syncthreads();
+  if (tid == 0) {              // -W (rows 0-63 of A1) and U are final
+    ptx::bulk_s2g(img_g + IMG_A1, img + IMG_A1, 16384);
+    ptx::bulk_s2g(img_g + IMG_U, img + IMG_U, IMG_F - IMG_U);
+    ptx::bulk_commit();
+  }
 
   // ---- 5. [E | F] = [Qbar | 0] + Aout [-W | U]; E over Qbar -----------------
   {
@@ -550,9 +665,10 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   ptx::fence_proxy_async_smem();
   __syncthreads();
 
-  // ---- 6. image -> workspace (bulk store through the TMA engine) -----------
-  if (tid == 0) {
-    ptx::bulk_s2g(ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES, img, IMG_BYTES);
+  // ---- 6. last part of the image -> workspace (bulk store, TMA engine) ----
+  if (tid == 0) {              // E and F; then every store must have read shared memory
+    ptx::bulk_s2g(img_g + IMG_A1 + 16384, img + IMG_A1 + 16384, 16384);
+    ptx::bulk_s2g(img_g + IMG_F, img + IMG_F, IMG_BYTES - IMG_F);
     ptx::bulk_commit();
     ptx::bulk_wait_read();
   }
@@ -745,7 +861,8 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
 #pragma unroll
         for (int g8 = 0; g8 < CW / 8; ++g8) {
           const int gg = pc * (CW / 8) + g8;
-          add8_f16(u + 8 * g8, *reinterpret_cast<const int4*>(ub + gg * 1024 + tid * 16));
+          add8_f16(u + 8 * g8, *reinterpret_cast<const int4*>(
+                                   ub + gg * 1024 + ((tid ^ ((v0 / 8 + gg) & 7)) << 4)));
           *reinterpret_cast<int4*>(Pb + gg * 1024 + (tid >> 3) * 128 + (tid & 7) * 16) =
               pack8_f16(u + 8 * g8);
         }
@@ -773,7 +890,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
       int4 fr[VS / 8];                                     // F row first: frees the stage early
 #pragma unroll
       for (int gg = 0; gg < VS / 8; ++gg)
-        fr[gg] = *reinterpret_cast<const int4*>(fb + gg * 1024 + c * 16);
+        fr[gg] = *reinterpret_cast<const int4*>(fb + gg * 1024 + ((c ^ ((v0 / 8 + gg) & 7)) << 4));
       ptx::mbar_arrive(fcons);                             // F of this stage consumed
 #pragma unroll
       for (int pc = 0; pc < NP; ++pc) {
@@ -863,9 +980,9 @@ cudaError_t launch_state(const ChunkParams& p, const uint8_t* ws, cudaStream_t s
   return cudaGetLastError();
 }
 
-template <typename TIO, bool VEC>
+template <typename TIO, int LOAD>
 cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
-  auto prep = prep_kernel<TIO, VEC>;
+  auto prep = prep_kernel<TIO, LOAD>;
   static bool attr_set = false;   // one attribute call per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -879,10 +996,25 @@ cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// every q/k/v/g row a 16-byte-aligned contiguous range (bulk-copy rules)
+template <typename TIO>
+bool bulk_rows_ok(const ChunkParams& p) {
+  auto al = [](const void* ptr, const int64_t* st, size_t esz) {
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    for (int d = 0; d < 3; ++d)
+      if ((st[d] * (int64_t)esz) % 16) return false;
+    return st[3] == 1;
+  };
+  return al(p.q, p.q_s, sizeof(TIO)) && al(p.k, p.k_s, sizeof(TIO)) &&
+         al(p.v, p.v_s, sizeof(TIO)) && al(p.g, p.g_s, 4);
+}
+
 template <typename TIO, typename TSI, typename TSO>
 cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   const bool vec = p.g_vec2 && p.qk_vec2 && p.v_vec2;
-  cudaError_t e = vec ? launch_prep<TIO, true>(p, ws, s) : launch_prep<TIO, false>(p, ws, s);
+  cudaError_t e = bulk_rows_ok<TIO>(p) ? launch_prep<TIO, 2>(p, ws, s)
+                  : vec                ? launch_prep<TIO, 1>(p, ws, s)
+                                       : launch_prep<TIO, 0>(p, ws, s);
   if (e != cudaSuccess) return e;
   switch (pick_vs(p)) {
     case 16: return launch_state<TIO, TSI, TSO, 16>(p, ws, s);

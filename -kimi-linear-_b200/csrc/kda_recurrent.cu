@@ -43,8 +43,9 @@ recurrent_kernel(const RecParams p) {
   // double-buffered per-step vectors: scaled q, k, alpha = exp(g)
   __shared__ float sq[2][kRecMaxK], sk[2][kRecMaxK], sa[2][kRecMaxK];
   __shared__ float sbeta[2];
-  // cross-warp partials: [warp][k^T AS (VT) | q^T AS (VT) | q.k]
-  __shared__ float red[NW][2 * VT + 1];
+  // cross-warp partials: [warp][k^T AS (VT) | q^T AS (VT) | q.k, pad]; rows
+  // padded to 16 bytes so the final sums read one float4 per warp and vector
+  __shared__ __align__(16) float red[NW][2 * VT + 4];
 
   float S[R][4];
   // ---- load the state tile (zeros when no initial state) -------------------
@@ -128,11 +129,10 @@ recurrent_kernel(const RecParams p) {
     float at[4] = {0.f, 0.f, 0.f, 0.f}, bt[4] = {0.f, 0.f, 0.f, 0.f}, qkt = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        at[c] += red[w][4 * ct + c];
-        bt[c] += red[w][VT + 4 * ct + c];
-      }
+      const float4 ra4 = *reinterpret_cast<const float4*>(&red[w][4 * ct]);
+      const float4 rb4 = *reinterpret_cast<const float4*>(&red[w][VT + 4 * ct]);
+      at[0] += ra4.x; at[1] += ra4.y; at[2] += ra4.z; at[3] += ra4.w;
+      bt[0] += rb4.x; bt[1] += rb4.y; bt[2] += rb4.z; bt[3] += rb4.w;
       qkt += red[w][2 * VT];
     }
     const float beta = sbeta[buf];

@@ -84,6 +84,27 @@ __device__ __forceinline__ void bulk_commit() {
 __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// wait until every committed bulk store except the newest N has read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_le() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// hint: bring one 128-byte line into L2 (no register result, never faults on
+// a valid address; used for the inputs of a CTA that will start later)
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+// hint: bring a 16-byte-aligned range (multiple of 16 bytes) into L2 through
+// the TMA engine; the issuing thread does not wait for it
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+// number of SMs of the device
+__device__ __forceinline__ uint32_t num_sms() {
+  uint32_t n;
+  asm volatile("mov.u32 %0, %%nsmid;" : "=r"(n));
+  return n;
+}
 // make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads, bulk copies)
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -83,12 +83,12 @@ __device__ __forceinline__ int a1_off(int m, int k) {
 __device__ __forceinline__ int a2_off(int m, int k) {
   return (m >> 3) * 1024 + (k >> 3) * 128 + (m & 7) * 16 + (k & 7) * 2;
 }
-// thread-read 64 x 128 layout of V, U and F: offset(c, v).  Each block of 8
-// value columns is 1 KiB (64 rows x 16 bytes); the row slot is XOR-swizzled
-// with the block index so that writers holding one row of many blocks and
-// readers holding many rows of one block both hit distinct banks.
+// 64 x 128 layout of V, U and F: offset(c, v).  Each block of 8 value columns
+// is 1 KiB (64 rows x 16 bytes).  For V this is the MN-major no-swizzle
+// operand layout of the phase-5 GEMM (core-matrix stride 128 bytes along the
+// chunk rows, 1 KiB along the value columns); U and F are read by threads.
 __device__ __forceinline__ int vb_off(int c, int v) {
-  return (v >> 3) * 1024 + ((c ^ ((v >> 3) & 7)) << 4) + (v & 7) * 2;
+  return (v >> 3) * 1024 + c * 16 + (v & 7) * 2;
 }
 // pack two fp32 as f16x2
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
@@ -133,9 +133,6 @@ __device__ __forceinline__ float2 ldg2(const T* p) {
 __device__ __forceinline__ void st_h2(uint8_t* base, int off, float a, float b) {
   *reinterpret_cast<__half2*>(base + off) = __floats2half2_rn(a, b);
 }
-__device__ __forceinline__ float2 ld_h2(const uint8_t* base, int off) {
-  return __half22float2(*reinterpret_cast<const __half2*>(base + off));
-}
 
 // ---------------------------------------------------------------------------
 // prep kernel
@@ -152,7 +149,10 @@ constexpr int P_LM = P_YB + CH * AXP * 4;              // L               fp32 [
 constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4]  fp32 [7][128]
 constexpr int P_BETA = P_FAC + 7 * KD * 4;             // beta            fp32 [64]
 constexpr int P_STEEP = P_BETA + CH * 4;               // steep bits      u32 [4][4]
-constexpr int PREP_SMEM = P_STEEP + 16 * 4;
+constexpr int P_MBAR = P_STEEP + 16 * 4;               // tcgen05 commit barrier (u64)
+constexpr int P_TSLOT = P_MBAR + 8;                    // TMEM base address (u32)
+constexpr int PREP_SMEM = P_TSLOT + 8;
+constexpr int kPrepTmemCols = 256;                     // D[128 x 256] fp32 of phase 5
 static_assert(P_A2 >= IMG_BYTES, "image staging");
 static_assert(PREP_SMEM <= 227 * 1024, "prep shared memory");
 // Aliases once their owners are dead: block decays Z[4][128] and exp(g_0)[128]
@@ -198,29 +198,6 @@ __device__ __forceinline__ void gemm16_3xtf32(float (*acc)[4], const float* Ab, 
   }
 }
 
-// acc(16 rows of block rb x 128 columns) = A[rows 16rb.., k < 16(rb+1)] * B, where A
-// is f16 K-major (a2_off geometry, row offset a_row0) and B is either the
-// K-major a1 geometry (k rows, 128 columns) or the vb geometry.
-template <bool B_IS_VB>
-__device__ __forceinline__ void gemm_rowblock_f16(float (*acc)[4], const uint8_t* A, int a_row0,
-                                                  const uint8_t* Bm, int rb, int lane) {
-  const int mi = lane >> 3;
-  for (int ks = 0; ks <= rb; ++ks) {
-    uint32_t a[4];
-    ptx::ldmatrix_x4(a, A + a2_off(a_row0 + 16 * rb + (lane & 7) + ((mi & 1) ? 8 : 0),
-                                   16 * ks + ((mi & 2) ? 8 : 0)));
-#pragma unroll
-    for (int nt = 0; nt < 16; nt += 2) {
-      uint32_t bq[4];
-      const int kr = 16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0);
-      const int kc = 8 * nt + ((mi & 2) ? 8 : 0);
-      ptx::ldmatrix_x4_trans(bq, Bm + (B_IS_VB ? vb_off(kr, kc) : a1_off(kr, kc)));
-      ptx::mma_f16_16x8x16(acc[nt], a, bq);
-      ptx::mma_f16_16x8x16(acc[nt + 1], a, bq + 2);
-    }
-  }
-}
-
 // LOAD: how phase 1 reads its inputs -- 0 scalar loads, 1 two-element vector
 // loads, 2 vector loads and, every input row being a 16-byte-aligned range,
 // the next wave's L2 prefetch issued as one bulk (TMA-engine) prefetch per row.
@@ -243,6 +220,8 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   float* Ef = P13 + KD;            // [4][128]  exp(-Z_r), 0 for steep channels
   float* sbeta = reinterpret_cast<float*>(sm + P_BETA);
   uint32_t* steep = reinterpret_cast<uint32_t*>(sm + P_STEEP);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_MBAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_TSLOT);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
@@ -259,6 +238,15 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
 
   if (tid < 16) steep[tid] = 0u;
   if (tid < CH) sbeta[tid] = (tid < nvalid) ? bb[(int64_t)(t0 + tid) * p.b_s[1]] : 0.f;
+  if (warp == 0) {                  // TMEM for phase 5 (one CTA per SM: never contended)
+    ptx::tmem_alloc(tslot, kPrepTmemCols);
+    ptx::tmem_relinquish();
+    ptx::tc_fence_before();
+  }
+  if (tid == 32) {
+    ptx::mbar_init(mbar, 1);
+    ptx::fence_mbar_init();
+  }
   uint8_t* img_g = ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES;
 
   // L2 prefetch of the inputs of the chunk one SM-count further in launch
@@ -390,7 +378,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     // transpose of four rows each lane owns one whole row of the group.
 #pragma unroll
     for (int i4 = 0; i4 < 16; i4 += 4) {
-      uint32_t qh[4], kh[4];
+      uint32_t qh[4], kh[4], vh[4];
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii) {
         const int i = i4 + ii, c = 16 * r + i;
@@ -399,14 +387,16 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
         const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;   // exp(gc_c)
         qh[ii] = pack_h2(qsx * egx, qsy * egy);                  // Qbar (-> E later)
         kh[ii] = pack_h2(kv.x * egx, kv.y * egy);                // Ktilde (-> -W later)
-        st_h2(img, IMG_U + vb_off(c, k0), vv.x, vv.y);           // V (-> U later)
+        vh[ii] = pack_h2(vv.x, vv.y);                            // V (-> U later)
         *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
         *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
         *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
       }
       quad_transpose(qh, tig);
       quad_transpose(kh, tig);
+      quad_transpose(vh, tig);
       const int c = 16 * r + i4 + tig;
+      *reinterpret_cast<uint4*>(img + IMG_U + vb_off(c, k0 & ~7)) = make_uint4(vh[0], vh[1], vh[2], vh[3]);
       *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(64 + c, k0 & ~7)) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
       *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(c, k0 & ~7)) = make_uint4(kh[0], kh[1], kh[2], kh[3]);
     }
@@ -605,72 +595,121 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   }
   __syncthreads();
 
-  // ---- 4. [W | U] = M [Ktilde | V]; store -W over Ktilde and U over V ------
+  // ---- 4. AM = Aout M over Aout (rows 64-127 of A2) -------------------------
+  // Aout M is block lower triangular like M: with it, one GEMM gives W, U,
+  // Aout W = AM Ktilde and F = Aout U = AM V.
   {
-    const int rb = warp & 3, half = warp >> 2;
-    float acc[16][4];
+    const int rb = warp & 3, ch = warp >> 2;             // row block, 32-column half
+    const int mi = lane >> 3;
+    float acc[4][4] = {};
+    for (int ks = 0; ks <= rb; ++ks) {
+      uint32_t a[4];
+      ptx::ldmatrix_x4(a, A2 + a2_off(64 + 16 * rb + (lane & 7) + ((mi & 1) ? 8 : 0),
+                                      16 * ks + ((mi & 2) ? 8 : 0)));
 #pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-    if (half == 0) gemm_rowblock_f16<false>(acc, A2, 0, img + IMG_A1, rb, lane);
-    else gemm_rowblock_f16<true>(acc, A2, 0, img + IMG_U, rb, lane);
-    __syncthreads();
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int row = 16 * rb + gid + 8 * hr, col = 8 * nt + 2 * tig;
-        if (half == 0)
-          st_h2(img, IMG_A1 + a1_off(row, col), -acc[nt][2 * hr], -acc[nt][2 * hr + 1]);
-        else
-          st_h2(img, IMG_U + vb_off(row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
+      for (int nt = 0; nt < 4; nt += 2) {
+        uint32_t bq[4];
+        ptx::ldmatrix_x4_trans(bq, A2 + a2_off(16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0),
+                                               32 * ch + 8 * nt + ((mi & 2) ? 8 : 0)));
+        ptx::mma_f16_16x8x16(acc[nt], a, bq);
+        ptx::mma_f16_16x8x16(acc[nt + 1], a, bq + 2);
       }
+    }
+    __syncthreads();                                     // every warp is done reading Aout
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr)
+        st_h2(A2, a2_off(64 + 16 * rb + gid + 8 * hr, 32 * ch + 8 * nt + 2 * tig),
+              acc[nt][2 * hr], acc[nt][2 * hr + 1]);
   }
-  ptx::fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {              // -W (rows 0-63 of A1) and U are final
-    ptx::bulk_s2g(img_g + IMG_A1, img + IMG_A1, 16384);
-    ptx::bulk_s2g(img_g + IMG_U, img + IMG_U, IMG_F - IMG_U);
-    ptx::bulk_commit();
-  }
-
-  // ---- 5. [E | F] = [Qbar | 0] + Aout [-W | U]; E over Qbar -----------------
-  {
-    const int rb = warp & 3, half = warp >> 2;
-    float acc[16][4];
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        float2 q0 = make_float2(0.f, 0.f);
-        if (half == 0) q0 = ld_h2(img, IMG_A1 + a1_off(64 + 16 * rb + gid + 8 * hr, 8 * nt + 2 * tig));
-        acc[nt][2 * hr] = q0.x;
-        acc[nt][2 * hr + 1] = q0.y;
-      }
-    if (half == 0) gemm_rowblock_f16<false>(acc, A2, 64, img + IMG_A1, rb, lane);
-    else gemm_rowblock_f16<true>(acc, A2, 64, img + IMG_U, rb, lane);
-    __syncthreads();
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int row = 16 * rb + gid + 8 * hr, col = 8 * nt + 2 * tig;
-        if (half == 0)
-          st_h2(img, IMG_A1 + a1_off(64 + row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
-        else
-          st_h2(img, IMG_F + vb_off(row, col), acc[nt][2 * hr], acc[nt][2 * hr + 1]);
-      }
-  }
-  ptx::fence_proxy_async_smem();
+  ptx::fence_proxy_async_smem();                         // A2, Ktilde, V -> tensor core
+  ptx::tc_fence_before();
   __syncthreads();
 
-  // ---- 6. last part of the image -> workspace (bulk store, TMA engine) ----
-  if (tid == 0) {              // E and F; then every store must have read shared memory
-    ptx::bulk_s2g(img_g + IMG_A1 + 16384, img + IMG_A1 + 16384, 16384);
-    ptx::bulk_s2g(img_g + IMG_F, img + IMG_F, IMG_BYTES - IMG_F);
-    ptx::bulk_commit();
-    ptx::bulk_wait_read();
+  // ---- 5. D[128 x 256] = [M; AM] [Ktilde | V] on tcgen05 (fp32 in TMEM) -----
+  //   rows 0-63:   [W | U]            rows 64-127: [Aout W | F]
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tslot;
+  if (warp == 0) {
+    if (ptx::elect_one()) {
+      const uint64_t dA = ptx::sdesc(ptx::smem_u32(A2), 128, 1024);            // K-major
+      const uint64_t dK = ptx::sdesc(ptx::smem_u32(img + IMG_A1), 2048, 128);  // MN-major
+      const uint64_t dV = ptx::sdesc(ptx::smem_u32(img + IMG_U), 128, 1024);   // MN-major
+      constexpr uint32_t ID = ptx::idesc_f16_f32(128, 128, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {                   // K = 64 chunk rows, 16 per MMA
+        ptx::mma_f16_ss(tbase, dA + 16 * ks, dK + 256 * ks, ID, ks > 0);
+        ptx::mma_f16_ss(tbase + 128, dA + 16 * ks, dV + 16 * ks, ID, ks > 0);
+      }
+      ptx::tc_commit(mbar);
+    }
+    __syncwarp();
+  }
+  const bool mma_ok = ptx::mbar_wait(mbar, 0, kWaitNs);
+  ptx::tc_fence_after();
+  if (__syncthreads_or(!mma_ok)) {                       // the GEMM never finished: give up
+    if (tid == 0) {
+      atomicExch(&g_kda_device_error, 2);
+      ptx::mbar_wait(mbar, 0, kWaitNs / 2);
+      ptx::bulk_wait_read();
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      ptx::tc_fence_after();
+      ptx::tmem_dealloc(tbase, kPrepTmemCols);
+    }
+    return;
+  }
+  {
+    // TMEM lane quarter of this warp = D rows 32 lq .. 32 lq + 31 (one per lane);
+    // warps 0-3 read columns 0-127, warps 4-7 columns 128-255
+    const int lq = warp & 3, row = 32 * lq + lane, half = warp >> 2;
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 128 * half;
+#pragma unroll 1
+    for (int pc = 0; pc < 4; ++pc) {
+      float v[32];
+      ptx::tmem_ld<32>(taddr + 32 * pc, v);
+      ptx::tmem_wait_ld();
+#pragma unroll
+      // ---- 6. straight from registers to the workspace image: a warp's 32
+      // rows of one 8-column group are four (A1) or one (U, F) whole 128-byte
+      // lines, so these 16-byte stores coalesce without staging
+      for (int o = 0; o < 4; ++o) {
+        const int col = 32 * pc + 8 * o;
+        float* x = v + 8 * o;
+        int off;
+        if (half == 0) {
+          off = IMG_A1 + a1_off(row, col);
+          if (row < 64) {                                  // -W
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = -x[e];
+          } else {                                         // E = Qbar - Aout W
+            const uint4 qv = *reinterpret_cast<const uint4*>(img + off);
+            const __half2* qh = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(qh[e]);
+              x[2 * e] = f.x - x[2 * e];
+              x[2 * e + 1] = f.y - x[2 * e + 1];
+            }
+          }
+        } else {                                           // U, F
+          off = row < 64 ? IMG_U + vb_off(row, col) : IMG_F + vb_off(row - 64, col);
+        }
+        *reinterpret_cast<uint4*>(img_g + off) =
+            make_uint4(pack_h2(x[0], x[1]), pack_h2(x[2], x[3]), pack_h2(x[4], x[5]),
+                       pack_h2(x[6], x[7]));
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (tid == 0) ptx::bulk_wait_read();   // the Kbar^T / d store must have read smem
+  if (warp == 0) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, kPrepTmemCols);
   }
 }
 
@@ -861,8 +900,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
 #pragma unroll
         for (int g8 = 0; g8 < CW / 8; ++g8) {
           const int gg = pc * (CW / 8) + g8;
-          add8_f16(u + 8 * g8, *reinterpret_cast<const int4*>(
-                                   ub + gg * 1024 + ((tid ^ ((v0 / 8 + gg) & 7)) << 4)));
+          add8_f16(u + 8 * g8, *reinterpret_cast<const int4*>(ub + gg * 1024 + tid * 16));
           *reinterpret_cast<int4*>(Pb + gg * 1024 + (tid >> 3) * 128 + (tid & 7) * 16) =
               pack8_f16(u + 8 * g8);
         }
@@ -890,7 +928,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
       int4 fr[VS / 8];                                     // F row first: frees the stage early
 #pragma unroll
       for (int gg = 0; gg < VS / 8; ++gg)
-        fr[gg] = *reinterpret_cast<const int4*>(fb + gg * 1024 + ((c ^ ((v0 / 8 + gg) & 7)) << 4));
+        fr[gg] = *reinterpret_cast<const int4*>(fb + gg * 1024 + c * 16);
       ptx::mbar_arrive(fcons);                             // F of this stage consumed
 #pragma unroll
       for (int pc = 0; pc < NP; ++pc) {

@@ -11,14 +11,15 @@ are independent, so there is no collective on the data path).
 Reported, all on the device with CUDA events on the launching stream:
 
 * ``value``     prefill tokens/s of the whole job (sum over ranks; time is the
-                max over ranks), L2 flushed before every step;
+                max over ranks); 4 rotating input sets (> 3x L2), no flush;
 * ``roofline``  the chunkwise kernel against measured HBM bandwidth (the
                 workload is HBM-bound: ~116 FLOP/B < ~255 FLOP/B ridge);
 * ``e2e``       the same metric through the public API from pinned host
                 buffers: H2D of q/k/v/g/beta and D2H of o and S inside the
                 timed region;
-* ``decode``    BASELINE configs[2]: B=64 recurrent single-token step on a
-                fp32 [64,16,128,128] state, captured in a CUDA graph and
+* ``decode``    BASELINE configs[2]: B=64 recurrent single-token steps on
+                fp32 [64,16,128,128] states, captured in a CUDA graph (four
+                steps on four distinct states: working set 4x L2) and
                 replayed, against HBM bandwidth;
 * ``long_context`` BASELINE configs[3]: B=8, T=32768 bf16 prefill with a
                 fp32 S0, (b, h) sharded over the ranks (strong scaling), with
@@ -50,7 +51,6 @@ METRIC = "KDA prefill & decode tokens/s per GPU (H16,d128); % of TC/HBM roofline
 CFG1 = dict(B=1, T=4096, H=16, K=128, V=128, C=64)
 CFG2 = dict(B=64, H=16, K=128, V=128)
 FLOP_PER_TOKEN_HEAD = 180224          # 2*[C(3K+2V) + 3KV] at C=64, K=V=128
-L2_FLUSH_BYTES = 512 << 20            # 4x the 126 MB L2
 
 
 def _peaks():
@@ -222,117 +222,132 @@ def cpu_port_throughput(t_sample, heads, steps=1, warmup=0):
 # --------------------------------------------------------------------------- #
 # GPU legs
 # --------------------------------------------------------------------------- #
-def _events_time(torch, fn, steps, warmup, flush, clk=None):
-    """Mean device ms of ``fn`` over ``steps`` runs, L2 flushed before each
-    (the flush is outside the events)."""
-    for _ in range(warmup):
-        fn()
+def _events_time(torch, fn, steps, warmup, clk=None, dist=None):
+    """Mean device ms of ``fn`` over ``steps`` runs (CUDA events on the
+    current stream), bracketed by synchronize + barrier on both sides.
+    Callers make sure the inputs of consecutive runs are not L2-resident
+    (rotating input sets or inputs larger than L2)."""
+    for i in range(warmup):
+        fn(i)
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     if clk is not None:
         clk.start()
     for i in range(steps):
-        flush.zero_()
         starts[i].record()
-        fn()
+        fn(i)
         ends[i].record()
     torch.cuda.synchronize()
     if clk is not None:
         clk.stop()
+    if dist is not None:
+        dist.barrier()
     return sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
 
 
-def bench_prefill(torch, kb, dev, steps, warmup, flush, dist, world, clk):
-    x = kb.synth.make_config(1, seed=0, device=dev)
-    q, k, v, g, beta = (x[n] for n in ("q", "k", "v", "g", "beta"))
+PREFILL_SETS = 4   # rotating input sets: 4 x 100 MB of inputs, plus outputs, > 3x L2
+
+
+def bench_prefill(torch, kb, dev, steps, warmup, dist, world, clk):
+    """Config 1.  Step i runs on input set i % PREFILL_SETS, so its inputs come
+    from HBM and the previous steps' outputs and workspace are written back
+    while it runs (the steady state of consecutive layers); no L2 flush."""
+    sets = [kb.synth.make_config(1, seed=s, device=dev) for s in range(PREFILL_SETS)]
     f32 = torch.float32
 
-    def step():
-        return kb.kda_chunkwise(q, k, v, g, beta, chunk_size=CFG1["C"], state_dtype=f32)
+    def step(i):
+        x = sets[i % PREFILL_SETS]
+        return kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"],
+                                chunk_size=CFG1["C"], state_dtype=f32)
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    clk.start()
-    for i in range(steps):
-        flush.zero_()
-        starts[i].record()
-        step()
-        ends[i].record()
-    torch.cuda.synchronize()
-    clk.stop()
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+    ms_step = _events_time(torch, step, steps, warmup, clk, dist)
+    total = torch.tensor([ms_step], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(total, op=dist.ReduceOp.MAX)
-    ms_step = total.item() / steps
+    ms_step = total.item()
 
     # end to end through the public API from pinned host memory
-    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", k), ("v", v), ("g", g),
-                                                  ("beta", beta))}
-    o_h = torch.empty((CFG1["B"], CFG1["T"], CFG1["H"], CFG1["V"]), dtype=v.dtype).pin_memory()
+    x0 = sets[0]
+    host = {n: x0[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
+    o_h = torch.empty((CFG1["B"], CFG1["T"], CFG1["H"], CFG1["V"]), dtype=x0["v"].dtype).pin_memory()
     S_h = torch.empty((CFG1["B"], CFG1["H"], CFG1["K"], CFG1["V"]), dtype=f32).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = o_h.numel() * o_h.element_size() + S_h.numel() * S_h.element_size()
 
-    def e2e_step():
+    def e2e_step(i):
         d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
         o, S = kb.kda_chunkwise(d["q"], d["k"], d["v"], d["g"], d["beta"],
                                 chunk_size=CFG1["C"], state_dtype=f32)
         o_h.copy_(o, non_blocking=True)
         S_h.copy_(S, non_blocking=True)
 
-    e2e_steps = max(5, steps // 4)
-    e2e_ms = _events_time(torch, e2e_step, e2e_steps, 3, flush, clk)
+    e2e_steps = max(5, steps // 10)
+    e2e_ms = _events_time(torch, e2e_step, e2e_steps, 3, clk, dist)
     e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    path = kb.chunkwise_path(q, k, v, g, beta, chunk_size=CFG1["C"], state_dtype=f32)
+    path = kb.chunkwise_path(x0["q"], x0["k"], x0["v"], x0["g"], x0["beta"],
+                             chunk_size=CFG1["C"], state_dtype=f32)
+    del sets
     return ms_step, e2e_t.item(), h2d, d2h, path
 
 
-def bench_decode(torch, kb, dev, steps, warmup, flush, clk):
-    """Config 2: one single-token recurrent step on a fp32 [64,16,128,128]
-    state, captured in a CUDA graph the way ``GraphedDecoder`` captures its
-    step (``graph_decode.py:269-289``: warm-up on a side stream, then
-    ``torch.cuda.graph``); the replay is timed with L2 flushed before each."""
+def bench_decode(torch, kb, dev, steps, warmup, clk):
+    """Config 2: single-token recurrent steps on fp32 [64,16,128,128] states,
+    captured in a CUDA graph the way ``GraphedDecoder`` captures its step
+    (``graph_decode.py:269-289``: warm-up on a side stream, then
+    ``torch.cuda.graph``).  The graph holds NBUF steps on NBUF distinct states
+    (inputs 4 x 64 MiB + outputs 4 x 64 MiB = 512 MiB, four times L2), so every
+    step reads its state from HBM and the previous steps' outputs are written
+    back while it runs -- the steady state of a decoder walking its layers,
+    with no L2 flush inside the timing.  Returns ms per step."""
+    NBUF = 4
     B, H, K, V = CFG2["B"], CFG2["H"], CFG2["K"], CFG2["V"]
     x = kb.synth.make_inputs(B, 1, H, K, V, dtype=torch.float16, seed=2, s0_std=0.02,
                              device=dev)
     args = [x[n] for n in ("q", "k", "v", "g", "beta")]
-    s0 = x["S0"]
+    states = [x["S0"].clone() for _ in range(NBUF)]
 
-    def step():
-        return kb.kda_recurrent(*args, state=s0, state_dtype=torch.float32)
+    def steps_all():
+        return [kb.kda_recurrent(*args, state=st, state_dtype=torch.float32) for st in states]
 
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
         for _ in range(3):
-            step()
+            steps_all()
     torch.cuda.current_stream(dev).wait_stream(side)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        o, S = step()
-    o_e, S_e = step()
+        outs = steps_all()
+    o_e, S_e = kb.kda_recurrent(*args, state=states[0], state_dtype=torch.float32)
     graph.replay()
     torch.cuda.synchronize()
-    assert torch.equal(o, o_e) and torch.equal(S, S_e), "graph replay differs from eager"
-    ms = _events_time(torch, graph.replay, steps, warmup, flush, clk)
+    assert torch.equal(outs[0][0], o_e) and torch.equal(outs[0][1], S_e), \
+        "graph replay differs from eager"
+    reps = max(1, steps // NBUF)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    clk.start()
+    for i in range(reps):
+        starts[i].record()
+        graph.replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clk.stop()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / (reps * NBUF)
     del graph
-    return ms
+    return ms, reps * NBUF
 
 
-def bench_long_context(torch, kb, dev, steps, warmup, flush, dist, world, rank, clk):
+def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
     """Config 3: B=8, T=32768, H=16 bf16 prefill with a fp32 S0, (b, h)
     sharded over the ranks (strong scaling), then o and S gathered to rank 0.
 
@@ -359,26 +374,25 @@ def bench_long_context(torch, kb, dev, steps, warmup, flush, dist, world, rank, 
     del full
     torch.cuda.empty_cache()
 
-    def step():
+    def step(i=0):
         return kb.kda_chunkwise(loc["q"], loc["k"], loc["v"], loc["g"], loc["beta"],
                                 initial_state=loc["S0"], chunk_size=c["C"],
                                 state_dtype=torch.float32)
 
-    ms = _events_time(torch, step, steps, warmup, flush, clk)
+    # inputs of 5.4 GB (one GPU) or 5.4/N GB per rank: far larger than L2
+    ms = _events_time(torch, step, steps, warmup, clk, dist)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = ms_t.item()
 
-    def step_gather():
+    def step_gather(i):
         o, S = step()
         kb.sharding.gather(o, (B, T, H, V), shard, "seq", dst=0)
         kb.sharding.gather(S, (B, H, K, V), shard, "state", dst=0)
 
     g_steps = max(2, steps // 2)
-    if dist is not None:
-        dist.barrier()
-    ms_g = _events_time(torch, step_gather, g_steps, 1, flush, clk)
+    ms_g = _events_time(torch, step_gather, g_steps, 1, clk, dist)
     ms_g_t = torch.tensor([ms_g], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(ms_g_t, op=dist.ReduceOp.MAX)
@@ -449,19 +463,18 @@ def main():
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                               device_id=dev)
         dist = td
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     with ClockSampler(dev.index) as clk:
         ms_step, e2e_ms, h2d, d2h, path = bench_prefill(
-            torch, kb, dev, a.steps, a.warmup, flush, dist, world, clk)
-        dec_ms = bench_decode(torch, kb, dev, a.decode_steps, a.warmup, flush, clk)
+            torch, kb, dev, a.steps, a.warmup, dist, world, clk)
+        dec_ms, dec_steps = bench_decode(torch, kb, dev, a.decode_steps, a.warmup, clk)
         dec_t = torch.tensor([dec_ms], dtype=torch.float64, device=dev)
         if dist is not None:
             dist.all_reduce(dec_t, op=dist.ReduceOp.MAX)
         dec_ms = dec_t.item()
         long_ctx = None
         if a.long_steps > 0:
-            long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, flush, dist, world,
+            long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, dist, world,
                                           rank, clk)
     clocks = clk.summary()
     # kernels per prefill call: prep + state pass on the tensor-core path
@@ -499,7 +512,8 @@ def main():
             "config": {"workload": "kda_chunkwise prefill, BASELINE configs[1] per GPU",
                        **CFG1, "state": "fp32", "parallelism": f"dp{world} over (b,h)",
                        "kernel": path,
-                       "l2": "flushed before every step (512 MiB write)"},
+                       "l2": "inputs larger than L2: 4 rotating input sets (400 MB) "
+                             "plus per-call outputs and workspace; no flush"},
             "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                          "frac": ach / hbm, "peak_kind": peak_kind,
                          "traffic": _traffic("kda_chunkwise", "cfg1"),
@@ -510,8 +524,10 @@ def main():
                     "ms_per_step": e2e_ms},
             "decode": {"workload": "kda_recurrent single-token step, BASELINE configs[2]",
                        "value": world * CFG2["B"] / (dec_ms * 1e-3), "unit": "tokens/s",
-                       "ms_per_step": dec_ms, "steps": a.decode_steps,
-                       "timing": "CUDA-graph replay of one step, L2 flushed before each",
+                       "ms_per_step": dec_ms, "steps": dec_steps,
+                       "timing": "CUDA graph of 4 single-token steps on 4 distinct "
+                                 "64 MiB states (512 MiB working set, 4x L2; no flush), "
+                                 "replayed; device time per step",
                        "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms * 1e-3) / 1e9,
                                     "peak": hbm, "unit": "GB/s",
                                     "frac": dec_bytes / (dec_ms * 1e-3) / 1e9 / hbm,

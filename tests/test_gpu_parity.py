@@ -222,6 +222,27 @@ def test_recurrent_decode_config2_vs_oracle(cuda_dev):
     assert rel(state, rS) < 1e-5
 
 
+def test_decode_full_config2_batch_one_step(cuda_dev):
+    """One decode step at the full config-2 batch (B=64, H=16, K=V=128, fp32
+    state): 2048 state tiles, several per persistent CTA, against the oracle;
+    then the same step from a state whose rows are not 16-byte aligned (the
+    guarded kernel) must agree with it."""
+    s = pkg().synth
+    x = s.make_inputs(64, 1, 16, 128, 128, dtype=torch.float16, seed=11, s0_std=0.02)
+    ro, rS = O.kda_recurrent(x["q"].numpy(), x["k"].numpy(), x["v"].numpy(), x["g"].numpy(),
+                             x["beta"].numpy(), state=x["S0"].numpy(), state_dtype="f32")
+    g = {k: v.to(cuda_dev) for k, v in x.items()}
+    o, S = pkg().kda_recurrent(g["q"], g["k"], g["v"], g["g"], g["beta"], state=g["S0"],
+                               state_dtype=torch.float32)
+    assert rel(o.float(), ro.astype(np.float32)) < 2e-3
+    assert rel(S, rS) < 1e-5
+    wide = torch.zeros(64, 16, 128, 129, device=cuda_dev)
+    wide[..., 1:] = g["S0"]
+    o2, S2 = pkg().kda_recurrent(g["q"], g["k"], g["v"], g["g"], g["beta"],
+                                 state=wide[..., 1:], state_dtype=torch.float32)
+    assert rel(S2, S) < 1e-6 and rel(o2.float(), o.float()) < 1e-3
+
+
 # --------------------------------------------------------------------------- #
 # edge cases
 # --------------------------------------------------------------------------- #

@@ -24,17 +24,19 @@ from __future__ import annotations
 
 import sys as _sys
 
-from . import _lib, ops, sharding, synth
+from . import _lib, fused, ops, sharding, synth
 from ._lib import KdaLibraryError
+from .fused import kda_epilogue, kda_prologue
 from .ops import KdaError, chunkwise_impl, chunkwise_path, device_error, kda_chunkwise, kda_recurrent
 
 ALIAS = "kimi_linear_b200"
 if __name__ != ALIAS:
     _sys.modules.setdefault(ALIAS, _sys.modules[__name__])
-    for _sub in ("_lib", "ops", "sharding", "synth"):
+    for _sub in ("_lib", "fused", "ops", "sharding", "synth"):
         _sys.modules.setdefault(f"{ALIAS}.{_sub}", _sys.modules[f"{__name__}.{_sub}"])
 
 __all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "chunkwise_impl", "device_error",
+           "kda_prologue", "kda_epilogue",
            "install", "uninstall",
            "KdaError", "KdaLibraryError", "load_library"]
 

@@ -42,6 +42,10 @@ EXPORTED = (
     "kda_status_string",
     "kda_device_supported",
     "kda_device_error",
+    "kda_prologue_fwd",
+    "kda_epilogue_fwd",
+    "kda_prologue_args_size",
+    "kda_epilogue_args_size",
     "kda_args_size",
     "kda_abi_version",
 )
@@ -76,6 +80,57 @@ class KdaArgs(ctypes.Structure):
     ]
 
 
+_I64x2 = ctypes.c_int64 * 2
+_P3 = ctypes.c_void_p * 3
+
+
+class KdaPrologueArgs(ctypes.Structure):
+    """Mirror of ``struct KdaPrologueArgs``."""
+
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("H", ctypes.c_int32),
+        ("K", ctypes.c_int32), ("V", ctypes.c_int32),
+        ("conv_size", ctypes.c_int32),
+        ("io_dtype", ctypes.c_int32),
+        ("gate_dtype", ctypes.c_int32),
+        ("l2norm_eps", ctypes.c_float),
+        ("q_in", ctypes.c_void_p), ("q_in_stride", _I64x2),
+        ("k_in", ctypes.c_void_p), ("k_in_stride", _I64x2),
+        ("v_in", ctypes.c_void_p), ("v_in_stride", _I64x2),
+        ("conv_w", _P3),
+        ("conv_b", _P3),
+        ("hist", _P3),
+        ("hist_batch_stride", _I64x3),
+        ("new_hist", _P3),
+        ("gk", ctypes.c_void_p), ("gk_stride", _I64x2),
+        ("beta_logit", ctypes.c_void_p), ("beta_logit_stride", _I64x2),
+        ("A_log", ctypes.c_void_p),
+        ("dt_bias", ctypes.c_void_p),
+        ("q", ctypes.c_void_p), ("q_stride", _I64x4),
+        ("k", ctypes.c_void_p), ("k_stride", _I64x4),
+        ("v", ctypes.c_void_p), ("v_stride", _I64x4),
+        ("g", ctypes.c_void_p), ("g_stride", _I64x4),
+        ("beta", ctypes.c_void_p), ("beta_stride", _I64x3),
+    ]
+
+
+class KdaEpilogueArgs(ctypes.Structure):
+    """Mirror of ``struct KdaEpilogueArgs``."""
+
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("H", ctypes.c_int32),
+        ("V", ctypes.c_int32),
+        ("io_dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float),
+        ("o", ctypes.c_void_p), ("o_stride", _I64x4),
+        ("og", ctypes.c_void_p), ("og_stride", _I64x2),
+        ("weight", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("y_stride", _I64x2),
+    ]
+
+
 class KdaLibraryError(RuntimeError):
     """The CUDA library is missing or unusable (there is no fallback path)."""
 
@@ -102,6 +157,14 @@ def _declare(lib):
     lib.kda_device_supported.restype = ctypes.c_int
     lib.kda_device_error.argtypes = [ctypes.c_int]
     lib.kda_device_error.restype = ctypes.c_int
+    lib.kda_prologue_fwd.argtypes = [ctypes.POINTER(KdaPrologueArgs), ctypes.c_void_p]
+    lib.kda_prologue_fwd.restype = ctypes.c_int
+    lib.kda_epilogue_fwd.argtypes = [ctypes.POINTER(KdaEpilogueArgs), ctypes.c_void_p]
+    lib.kda_epilogue_fwd.restype = ctypes.c_int
+    lib.kda_prologue_args_size.argtypes = []
+    lib.kda_prologue_args_size.restype = ctypes.c_size_t
+    lib.kda_epilogue_args_size.argtypes = []
+    lib.kda_epilogue_args_size.restype = ctypes.c_size_t
     lib.kda_args_size.argtypes = []
     lib.kda_args_size.restype = ctypes.c_size_t
     lib.kda_abi_version.argtypes = []
@@ -129,6 +192,10 @@ def load(path: str | None = None):
         _declare(lib)
         if lib.kda_abi_version() != ABI_VERSION:
             raise KdaLibraryError(f"{p}: ABI version {lib.kda_abi_version()} != {ABI_VERSION}")
+        for fn, st in (("kda_prologue_args_size", KdaPrologueArgs),
+                       ("kda_epilogue_args_size", KdaEpilogueArgs)):
+            if getattr(lib, fn)() != ctypes.sizeof(st):
+                raise KdaLibraryError(f"{p}: {fn}() != ctypes sizeof {ctypes.sizeof(st)}")
         if lib.kda_args_size() != ctypes.sizeof(KdaArgs):
             raise KdaLibraryError(
                 f"{p}: sizeof(KdaArgs) {lib.kda_args_size()} != ctypes {ctypes.sizeof(KdaArgs)}")

@@ -138,6 +138,77 @@ int launch_status(cudaError_t e) {
              : KDA_ERR_CUDA;
 }
 
+int validate_prologue(const KdaPrologueArgs* a) {
+  if (a == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
+  if (a->B < 0 || a->T < 0 || a->H < 0) return KDA_ERR_SHAPE;
+  if (a->K != a->V || (a->K != 32 && a->K != 64 && a->K != 128)) return KDA_ERR_SHAPE;
+  if (a->conv_size < 1 || a->conv_size > 4) return KDA_ERR_SHAPE;
+  if (!dtype_ok(a->io_dtype) || !dtype_ok(a->gate_dtype)) return KDA_ERR_DTYPE;
+  if (!(a->l2norm_eps > 0.f)) return KDA_ERR_SHAPE;
+  if (!a->q_in || !a->k_in || !a->v_in || !a->gk || !a->beta_logit || !a->A_log ||
+      !a->dt_bias || !a->q || !a->k || !a->v || !a->g || !a->beta)
+    return KDA_ERR_NULL_POINTER;
+  for (int i = 0; i < 3; ++i)
+    if (!a->conv_w[i]) return KDA_ERR_NULL_POINTER;
+  if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->g_stride[3] != 1 ||
+      a->beta_stride[2] != 1)
+    return KDA_ERR_STRIDE;
+  return KDA_OK;
+}
+
+PrologueParams to_prologue(const KdaPrologueArgs* a) {
+  PrologueParams p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.K = a->K; p.V = a->V;
+  p.conv_size = a->conv_size;
+  p.io_dtype = a->io_dtype; p.gate_dtype = a->gate_dtype;
+  p.eps = a->l2norm_eps;
+  p.q_in = a->q_in; p.k_in = a->k_in; p.v_in = a->v_in;
+  for (int d = 0; d < 2; ++d) {
+    p.in_s[0][d] = a->q_in_stride[d];
+    p.in_s[1][d] = a->k_in_stride[d];
+    p.in_s[2][d] = a->v_in_stride[d];
+    p.gk_s[d] = a->gk_stride[d];
+    p.bl_s[d] = a->beta_logit_stride[d];
+  }
+  p.w_q = a->conv_w[0]; p.w_k = a->conv_w[1]; p.w_v = a->conv_w[2];
+  p.b_q = a->conv_b[0]; p.b_k = a->conv_b[1]; p.b_v = a->conv_b[2];
+  p.hist_q = a->hist[0]; p.hist_k = a->hist[1]; p.hist_v = a->hist[2];
+  for (int i = 0; i < 3; ++i) p.hist_bs[i] = a->hist_batch_stride[i];
+  p.new_q = a->new_hist[0]; p.new_k = a->new_hist[1]; p.new_v = a->new_hist[2];
+  p.gk = a->gk; p.beta_logit = a->beta_logit;
+  p.A_log = a->A_log; p.dt_bias = a->dt_bias;
+  p.q = a->q; p.k = a->k; p.v = a->v;
+  std::memcpy(p.out_s[0], a->q_stride, sizeof(p.out_s[0]));
+  std::memcpy(p.out_s[1], a->k_stride, sizeof(p.out_s[1]));
+  std::memcpy(p.out_s[2], a->v_stride, sizeof(p.out_s[2]));
+  p.g = a->g; std::memcpy(p.g_s, a->g_stride, sizeof(p.g_s));
+  p.beta = a->beta; std::memcpy(p.beta_s, a->beta_stride, sizeof(p.beta_s));
+  return p;
+}
+
+int validate_epilogue(const KdaEpilogueArgs* a) {
+  if (a == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
+  if (a->B < 0 || a->T < 0 || a->H < 0) return KDA_ERR_SHAPE;
+  if (a->V < 32 || a->V > 128 || a->V % 32 != 0) return KDA_ERR_SHAPE;
+  if (!dtype_ok(a->io_dtype)) return KDA_ERR_DTYPE;
+  if (!(a->eps >= 0.f)) return KDA_ERR_SHAPE;
+  if (!a->o || !a->og || !a->weight || !a->y) return KDA_ERR_NULL_POINTER;
+  if (a->o_stride[3] != 1) return KDA_ERR_STRIDE;
+  return KDA_OK;
+}
+
+EpilogueParams to_epilogue(const KdaEpilogueArgs* a) {
+  EpilogueParams p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.V = a->V; p.io_dtype = a->io_dtype; p.eps = a->eps;
+  p.o = a->o; std::memcpy(p.o_s, a->o_stride, sizeof(p.o_s));
+  p.og = a->og; std::memcpy(p.og_s, a->og_stride, sizeof(p.og_s));
+  p.weight = a->weight;
+  p.y = a->y; std::memcpy(p.y_s, a->y_stride, sizeof(p.y_s));
+  return p;
+}
+
 }  // namespace
 }  // namespace kda
 
@@ -214,6 +285,28 @@ int kda_device_supported(int device) {
 }
 
 int kda_device_error(int clear) { return read_device_error(clear != 0); }
+
+int kda_prologue_fwd(const KdaPrologueArgs* args, void* stream) {
+  int st = validate_prologue(args);
+  if (st != KDA_OK) return st;
+  if (args->B == 0 || args->T == 0 || args->H == 0) return KDA_OK;
+  st = check_arch();
+  if (st != KDA_OK) return st;
+  return launch_status(launch_prologue(to_prologue(args), static_cast<cudaStream_t>(stream)));
+}
+
+int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream) {
+  int st = validate_epilogue(args);
+  if (st != KDA_OK) return st;
+  if (args->B == 0 || args->T == 0 || args->H == 0) return KDA_OK;
+  st = check_arch();
+  if (st != KDA_OK) return st;
+  return launch_status(launch_epilogue(to_epilogue(args), static_cast<cudaStream_t>(stream)));
+}
+
+size_t kda_prologue_args_size(void) { return sizeof(KdaPrologueArgs); }
+
+size_t kda_epilogue_args_size(void) { return sizeof(KdaEpilogueArgs); }
 
 size_t kda_args_size(void) { return sizeof(KdaArgs); }
 

@@ -33,6 +33,40 @@ struct RecParams {
 
 using ChunkParams = RecParams;
 
+// Device-side view of KdaPrologueArgs (strides in elements).
+struct PrologueParams {
+  int B, T, H, K, V, conv_size;
+  int io_dtype, gate_dtype;
+  float eps;
+  const void *q_in, *k_in, *v_in;
+  int64_t in_s[3][2];                  // (batch, time) strides of q_in, k_in, v_in
+  const float *w_q, *w_k, *w_v;        // [D, conv_size]
+  const float *b_q, *b_k, *b_v;        // [D] or null
+  const void *hist_q, *hist_k, *hist_v;
+  int64_t hist_bs[3];                  // batch strides of the histories
+  void *new_q, *new_k, *new_v;         // [B, conv_size - 1, D] contiguous, or null
+  const void* gk; int64_t gk_s[2];
+  const void* beta_logit; int64_t bl_s[2];
+  const float *A_log, *dt_bias;        // [H, K]
+  void *q, *k, *v;
+  int64_t out_s[3][4];
+  float* g; int64_t g_s[4];
+  float* beta; int64_t beta_s[3];
+};
+
+// Device-side view of KdaEpilogueArgs.
+struct EpilogueParams {
+  int B, T, H, V, io_dtype;
+  float eps;
+  const void* o; int64_t o_s[4];
+  const void* og; int64_t og_s[2];
+  const float* weight;
+  void* y; int64_t y_s[2];
+};
+
+cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t s);
+cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s);
+
 cudaError_t launch_recurrent(const RecParams& p, cudaStream_t s);
 cudaError_t launch_chunk_simt(const ChunkParams& p, cudaStream_t s);
 bool chunk_tc_supported(const ChunkParams& p);

@@ -1,0 +1,213 @@
+// kda_io.cu -- fused prologue and epilogue of the KDA block for sm_100a.
+//
+// Prologue (replaces the elementwise part of KimiDeltaAttention._projections,
+// kimi_linear/kda.py:399-461, after the projection GEMMs):
+//   q, k, v = l2norm(silu(ShortConv(q_in))), l2norm(silu(ShortConv(k_in))),
+//             silu(ShortConv(v_in))                      (kda.py:282-325,446-450)
+//   g       = -exp(A_log) * softplus(gk + dt_bias)       (kda.py:455-460)
+//   beta    = sigmoid(beta_logit)                        (kda.py:452)
+//   plus the new conv cache (the last conv_size - 1 inputs, kda.py:427-440).
+// The reference runs ~10 separate passes over HBM for this; here one CTA per
+// (b, head, 64-token tile, tensor) reads each input once and writes each
+// output once.  The causal conv of a channel is a sliding window in
+// registers (thread = channel); the per-token L2 norm is a warp reduction
+// over the head dimension staged in shared memory.
+//
+// Epilogue (KimiDeltaAttention._output before o_proj, kda.py:464-470, with
+// HeadwiseRMSNorm kda.py:258-279):
+//   o = (rmsnorm_head(o_core) * w).to(dtype);  o = (o * sigmoid(og)).to(dtype)
+// one warp per (b, t, h) row.
+//
+// Rounding follows the reference's fp16/bf16 path: the conv output, the SiLU
+// output and the RMSNorm output are rounded to the I/O dtype where the
+// reference materialises them in that dtype; reductions are fp32.
+#include "kda_internal.cuh"
+
+namespace kda {
+namespace io {
+
+constexpr int TT = 64;   // tokens per prologue CTA
+
+// x rounded to T and back (identity for fp32)
+template <typename T> __device__ __forceinline__ float rnd(float x);
+template <> __device__ __forceinline__ float rnd<float>(float x) { return x; }
+template <> __device__ __forceinline__ float rnd<__half>(float x) {
+  return __half2float(__float2half_rn(x));
+}
+template <> __device__ __forceinline__ float rnd<__nv_bfloat16>(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
+// torch.nn.functional.softplus with beta = 1, threshold = 20
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
+
+// blockIdx.x: token tile, blockIdx.y: tensor * H + head (tensor 0 q, 1 k, 2 v,
+// 3 gates), blockIdx.z: batch.  blockDim.x = head dim (32, 64 or 128).
+template <typename TIO, typename TG>
+__global__ void __launch_bounds__(128)
+prologue_kernel(const PrologueParams p) {
+  __shared__ float ys[TT][128 + 1];
+  __shared__ float rstd[TT];
+  const int c = threadIdx.x;                       // channel within the head
+  const int HD = blockDim.x;
+  const int tensor = blockIdx.y / p.H, h = blockIdx.y - tensor * p.H;
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * TT;
+  const int nt = min(TT, p.T - t0);
+  const int lane = c & 31, warp = c >> 5, nw = HD >> 5;
+
+  if (tensor == 3) {                               // decay and beta gates
+    const int ch = h * p.K + c;
+    if (c < p.K) {
+      const float a = -expf(p.A_log[ch]);
+      const float dtb = p.dt_bias[ch];
+      const TG* gk = static_cast<const TG*>(p.gk) + b * p.gk_s[0] + ch;
+      float* g = p.g + b * p.g_s[0] + h * p.g_s[2] + c;
+      for (int i = 0; i < nt; ++i) {
+        const int t = t0 + i;
+        g[(int64_t)t * p.g_s[1]] = a * softplus(ld(gk + (int64_t)t * p.gk_s[1]) + dtb);
+      }
+    }
+    for (int i = c; i < nt; i += blockDim.x) {         // beta: every token of the tile
+      const int t = t0 + i;
+      const TG* bl = static_cast<const TG*>(p.beta_logit) + b * p.bl_s[0] + (int64_t)t * p.bl_s[1] + h;
+      p.beta[b * p.beta_s[0] + (int64_t)t * p.beta_s[1] + h] = sigmoidf(ld(bl));
+    }
+    return;
+  }
+
+  const int D = tensor == 2 ? p.H * p.V : p.H * p.K;
+  const int ch = h * HD + c;                       // channel in [0, D)
+  const TIO* x = static_cast<const TIO*>(tensor == 0 ? p.q_in : tensor == 1 ? p.k_in : p.v_in) +
+                 b * p.in_s[tensor][0] + ch;
+  const int64_t xs = p.in_s[tensor][1];
+  const TIO* hist = static_cast<const TIO*>(tensor == 0 ? p.hist_q : tensor == 1 ? p.hist_k : p.hist_v);
+  const float* w = (tensor == 0 ? p.w_q : tensor == 1 ? p.w_k : p.w_v) + (int64_t)ch * p.conv_size;
+  const float* bias = tensor == 0 ? p.b_q : tensor == 1 ? p.b_k : p.b_v;
+  const int cs = p.conv_size, keep = cs - 1;
+
+  // input at time t (t < 0 reads the conv history, or zero without one)
+  auto xin = [&](int t) -> float {
+    if (t >= 0) return ld(x + (int64_t)t * xs);
+    if (hist == nullptr) return 0.f;
+    return ld(hist + b * p.hist_bs[tensor] + (int64_t)(keep + t) * D + ch);
+  };
+  // a fixed four-tap window: after the shift of step i, win[j] = x(t0+i-3+j);
+  // the conv_size taps sit at its right end and the rest are never used
+  // (static register indexing).  Before the first shift slots 1-3 hold
+  // x(t0-3 .. t0-1).
+  float wr[4], win[4];
+  const float bv = bias ? bias[ch] : 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    wr[j] = (j >= 4 - cs) ? w[j - (4 - cs)] : 0.f;
+    win[j] = (j >= 1 && j - 1 >= 4 - cs) ? xin(t0 - 4 + j) : 0.f;
+  }
+  for (int i = 0; i < nt; ++i) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) win[j] = win[j + 1];
+    win[3] = xin(t0 + i);
+    float acc = bv;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j >= 4 - cs) acc = fmaf(win[j], wr[j], acc);
+    // conv output in the I/O dtype, SiLU of it, again in the I/O dtype
+    ys[i][c] = rnd<TIO>(silu(rnd<TIO>(acc)));
+  }
+  // new conv cache: the last keep inputs of cat(history, x)
+  if (p.new_q != nullptr && t0 + nt == p.T && keep > 0) {
+    TIO* nc = static_cast<TIO*>(tensor == 0 ? p.new_q : tensor == 1 ? p.new_k : p.new_v) +
+              b * (int64_t)keep * D + ch;
+    for (int j = 0; j < keep; ++j) st(nc + (int64_t)j * D, xin(p.T - keep + j));
+  }
+  __syncthreads();
+
+  const bool norm = tensor < 2;
+  if (norm) {                                      // per-token L2 norm over the head
+    for (int i = warp; i < nt; i += nw) {
+      float ss = 0.f;
+      for (int cc = lane; cc < HD; cc += 32) ss = fmaf(ys[i][cc], ys[i][cc], ss);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) rstd[i] = fminf(rsqrtf(ss), 1.f / p.eps);
+    }
+    __syncthreads();
+  }
+  TIO* out = static_cast<TIO*>(tensor == 0 ? p.q : tensor == 1 ? p.k : p.v) +
+             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + c;
+  const int64_t os = p.out_s[tensor][1];
+  for (int i = 0; i < nt; ++i) {
+    const float y = norm ? ys[i][c] * rstd[i] : ys[i][c];
+    st(out + (int64_t)(t0 + i) * os, y);
+  }
+}
+
+// one warp per (b, t, h) row of V channels (V <= 128, multiple of 32)
+template <typename TIO>
+__global__ void __launch_bounds__(256)
+epilogue_kernel(const EpilogueParams p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long rows = (long)p.B * p.T * p.H;
+  if (warp >= rows) return;
+  const int h = warp % p.H;
+  const long bt = warp / p.H;
+  const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+  const TIO* o = static_cast<const TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] + h * p.o_s[2];
+  const TIO* og = static_cast<const TIO*>(p.og) + b * p.og_s[0] + (int64_t)t * p.og_s[1] + h * p.V;
+  TIO* y = static_cast<TIO*>(p.y) + b * p.y_s[0] + (int64_t)t * p.y_s[1] + h * p.V;
+  const float* w = p.weight + h * p.V;
+  float xv[4] = {0.f, 0.f, 0.f, 0.f};
+  float ss = 0.f;
+  const int n = p.V >> 5;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j < n) xv[j] = ld(o + lane + 32 * j);
+    ss = fmaf(xv[j], xv[j], ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(ss / p.V + p.eps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= n) break;
+    const int cc = lane + 32 * j;
+    const float nrm = rnd<TIO>(xv[j] * r * w[cc]);                 // g_norm output dtype
+    st(y + cc, nrm * sigmoidf(ld(og + cc)));                       // gate in fp32, round once
+  }
+}
+
+template <typename TIO>
+static cudaError_t launch_pro_t(const PrologueParams& p, cudaStream_t s) {
+  dim3 grid((p.T + TT - 1) / TT, 4 * p.H, p.B);
+  const int threads = p.K;   // K == V enforced by the caller
+  if (p.gate_dtype == KDA_DTYPE_F32) prologue_kernel<TIO, float><<<grid, threads, 0, s>>>(p);
+  else if (p.gate_dtype == KDA_DTYPE_F16) prologue_kernel<TIO, __half><<<grid, threads, 0, s>>>(p);
+  else prologue_kernel<TIO, __nv_bfloat16><<<grid, threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace io
+
+cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t s) {
+  switch (p.io_dtype) {
+    case KDA_DTYPE_F32: return io::launch_pro_t<float>(p, s);
+    case KDA_DTYPE_F16: return io::launch_pro_t<__half>(p, s);
+    default: return io::launch_pro_t<__nv_bfloat16>(p, s);
+  }
+}
+
+cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s) {
+  const long rows = (long)p.B * p.T * p.H;
+  const int threads = 256;
+  const long blocks = (rows * 32 + threads - 1) / threads;
+  switch (p.io_dtype) {
+    case KDA_DTYPE_F32: io::epilogue_kernel<float><<<blocks, threads, 0, s>>>(p); break;
+    case KDA_DTYPE_F16: io::epilogue_kernel<__half><<<blocks, threads, 0, s>>>(p); break;
+    default: io::epilogue_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p); break;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace kda

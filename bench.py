@@ -410,6 +410,29 @@ def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
                          "unit": "GB/s", "algorithmic_bytes": byts}}
 
 
+def profile_case(which, reps=3):
+    """Three calls of one workload on cuda:0 (the target of the ncu captures
+    summarised under profiles/): ``prefill`` = configs[1], ``decode`` = one
+    configs[2] step."""
+    import torch
+    kb = importlib.import_module("-kimi-linear-_b200")
+    kb.load_library()
+    dev = torch.device("cuda", 0)
+    if which == "prefill":
+        x = kb.synth.make_config(1, seed=0, device=dev)
+        for _ in range(reps):
+            kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=CFG1["C"],
+                             state_dtype=torch.float32)
+    else:
+        y = kb.synth.make_inputs(CFG2["B"], 1, CFG2["H"], CFG2["K"], CFG2["V"],
+                                 dtype=torch.float16, seed=2, s0_std=0.02, device=dev)
+        for _ in range(reps):
+            kb.kda_recurrent(y["q"], y["k"], y["v"], y["g"], y["beta"], state=y["S0"],
+                             state_dtype=torch.float32)
+    torch.cuda.synchronize()
+    print(f"case {which}: {reps} calls done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,7 +443,11 @@ def main():
     ap.add_argument("--long-steps", type=int, default=4,
                     help="timed steps of the configs[3] leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=("prefill", "decode"),
+                    help="profiling target: run the workload three times, print nothing timed")
     a = ap.parse_args()
+    if a.case:
+        return profile_case(a.case)
     if a.warmup < 3:
         a.warmup = 3
 

@@ -145,6 +145,84 @@ int kda_device_supported(int device);
  */
 int kda_device_error(int clear);
 
+/*
+ * Prologue of the KDA block after its projection GEMMs: causal depthwise
+ * ShortConv (conv_size <= 4, optional bias, optional conv history) and SiLU of
+ * q_in / k_in / v_in, per-head L2 normalisation of q and k (fp32 reduction,
+ * rsqrt clamped at 1 / l2norm_eps), the log decay
+ * g = -exp(A_log) * softplus(gk + dt_bias) and beta = sigmoid(beta_logit).
+ * Reference: the elementwise part of KimiDeltaAttention._projections,
+ * kimi_linear/kda.py:399-461 (ShortConv kda.py:282-310, l2norm kda.py:313-325),
+ * for both its batch path and its single-token decode path (conv history =
+ * the module's conv cache).  One pass over HBM instead of the reference's
+ * separate elementwise passes.
+ *
+ * Layouts (strides in elements, innermost stride 1):
+ *   q_in, k_in : [B, T, H*K]   v_in : [B, T, H*V]   gk : [B, T, H*K]
+ *   beta_logit : [B, T, H]     (stride pairs are (batch, time))
+ *   conv_w[i]  : [D, conv_size] fp32 contiguous (nn.Conv1d weight [D, 1, cs])
+ *   conv_b[i]  : [D] fp32 or NULL;  A_log, dt_bias : [H, K] fp32 contiguous
+ *   hist[i]    : conv history [B, conv_size-1, D] (time stride D, batch
+ *                stride hist_batch_stride[i]) or NULL for zeros
+ *   new_hist[i]: [B, conv_size-1, D] contiguous output, or NULL
+ *   q, k : [B, T, H, K]  v : [B, T, H, V]  (io_dtype);  g : [B, T, H, K] fp32;
+ *   beta : [B, T, H] fp32.   Index i: 0 = q, 1 = k, 2 = v.
+ * Requires K == V in {32, 64, 128}.
+ */
+typedef struct KdaPrologueArgs {
+  int32_t abi_version;
+  int32_t B, T, H, K, V;
+  int32_t conv_size;                 /* 1..4 */
+  int32_t io_dtype;                  /* q_in/k_in/v_in, histories, q/k/v */
+  int32_t gate_dtype;                /* gk and beta_logit */
+  float l2norm_eps;
+  const void* q_in; int64_t q_in_stride[2];
+  const void* k_in; int64_t k_in_stride[2];
+  const void* v_in; int64_t v_in_stride[2];
+  const float* conv_w[3];
+  const float* conv_b[3];
+  const void* hist[3];
+  int64_t hist_batch_stride[3];
+  void* new_hist[3];
+  const void* gk; int64_t gk_stride[2];
+  const void* beta_logit; int64_t beta_logit_stride[2];
+  const float* A_log;
+  const float* dt_bias;
+  void* q; int64_t q_stride[4];
+  void* k; int64_t k_stride[4];
+  void* v; int64_t v_stride[4];
+  float* g; int64_t g_stride[4];
+  float* beta; int64_t beta_stride[3];
+} KdaPrologueArgs;
+
+int kda_prologue_fwd(const KdaPrologueArgs* args, void* stream);
+
+/*
+ * Epilogue of the KDA block before o_proj: head-wise RMSNorm of o (fp32,
+ * per-head weight [H, V]) rounded to io_dtype, times sigmoid(og) in fp32,
+ * rounded to io_dtype.  Reference: KimiDeltaAttention._output without its
+ * o_proj GEMM, kimi_linear/kda.py:464-470, and HeadwiseRMSNorm
+ * kimi_linear/kda.py:258-279.
+ *   o : [B, T, H, V] (strides in elements)   og, y : [B, T, H*V] (batch, time)
+ * Requires V in {32, 64, 96, 128}.
+ */
+typedef struct KdaEpilogueArgs {
+  int32_t abi_version;
+  int32_t B, T, H, V;
+  int32_t io_dtype;
+  float eps;
+  const void* o; int64_t o_stride[4];
+  const void* og; int64_t og_stride[2];
+  const float* weight;               /* [H, V] fp32 contiguous */
+  void* y; int64_t y_stride[2];
+} KdaEpilogueArgs;
+
+int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream);
+
+/* sizeof(KdaPrologueArgs) / sizeof(KdaEpilogueArgs) as compiled. */
+size_t kda_prologue_args_size(void);
+size_t kda_epilogue_args_size(void);
+
 /* sizeof(KdaArgs) as compiled, for FFI layout checks. */
 size_t kda_args_size(void);
 

@@ -31,7 +31,24 @@ def pkg():
 
 
 def golden_cases():
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
+    """Golden cases of the KDA core (tests/golden/make_golden.py)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
+                  if not os.path.basename(p).startswith("fused_"))
+
+
+def fused_cases():
+    """Golden cases of the fused prologue / epilogue (make_golden_fused.py)."""
+    return sorted(os.path.basename(p)[:-4]
+                  for p in glob.glob(os.path.join(GOLDEN, "fused_*.npz")))
+
+
+def load_fused(name):
+    """Fused golden case ``name``: dict of numpy arrays plus ``meta`` (a dict)."""
+    import json
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    d = {k: z[k] for k in z.files}
+    d["meta"] = json.loads(str(d["meta"]))
+    return d
 
 
 def load_golden(name):

@@ -114,3 +114,32 @@ def test_reference_module_routes_through_patch():
             assert mod(x).shape == x.shape   # the reference path again
     finally:
         sys.path.remove(REF)
+
+
+def test_install_module_patches_and_restores_methods():
+    """install_module routes a KimiDeltaAttention-like class's _projections /
+    _output through the fused drop-ins; uninstall_module restores them."""
+    kb = pkg()
+
+    class FakeKDA:
+        def _projections(self, x, conv_cache=None, use_cache=False):
+            return "reference-projections"
+
+        def _output(self, o_core, x):
+            return "reference-output"
+
+    orig_p, orig_o = FakeKDA._projections, FakeKDA._output
+    kb.fused.install_module(FakeKDA)
+    try:
+        assert FakeKDA._projections is kb.fused.projections
+        assert FakeKDA._output is kb.fused.output
+    finally:
+        kb.fused.uninstall_module()
+    assert FakeKDA._projections is orig_p and FakeKDA._output is orig_o
+
+
+def test_fused_cpu_tensors_raise():
+    kb = pkg()
+    x = torch.zeros(1, 4, 64)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        kb.kda_epilogue(torch.zeros(1, 4, 2, 32), x, torch.ones(2, 32), 1e-6)

@@ -36,6 +36,7 @@ if __name__ != ALIAS:
         _sys.modules.setdefault(f"{ALIAS}.{_sub}", _sys.modules[f"{__name__}.{_sub}"])
 
 __all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "chunkwise_impl", "device_error",
+           "kda_chunkwise_inplace", "kda_recurrent_inplace",
            "kda_prologue", "kda_epilogue",
            "install", "uninstall",
            "KdaError", "KdaLibraryError", "load_library"]
@@ -49,7 +50,19 @@ def load_library():
 _saved = []
 
 
-def install(kda_module=None, package=None):
+def kda_chunkwise_inplace(q, k, v, g, beta, initial_state=None, chunk_size=64, tile_size=0,
+                          state_dtype=None):
+    """``kda_chunkwise`` that updates ``initial_state`` in place (when given)."""
+    return kda_chunkwise(q, k, v, g, beta, initial_state, chunk_size, tile_size, state_dtype,
+                         inplace=True)
+
+
+def kda_recurrent_inplace(q, k, v, g, beta, state=None, state_dtype=None):
+    """``kda_recurrent`` that updates ``state`` in place (when given)."""
+    return kda_recurrent(q, k, v, g, beta, state, state_dtype, inplace=True)
+
+
+def install(kda_module=None, package=None, inplace_state=False):
     """Point the reference's KDA kernels at this package.
 
     Replaces ``kda_chunkwise`` / ``kda_recurrent`` in ``kimi_linear.kda`` (or the
@@ -58,6 +71,14 @@ def install(kda_module=None, package=None):
     CUDA library first, so a missing build fails here rather than mid-model.
     Returns the list of patched ``(module, name)`` pairs; :func:`uninstall`
     restores the originals.
+
+    ``inplace_state=True`` installs the in-place variants: the recurrent state
+    passed in is overwritten with the new one (the reference returns a fresh
+    tensor and leaves the old one intact, ``kda.py:137,205``).  The model's
+    own cache handling replaces the old state with the returned one, so
+    decoding is unchanged, and ``GraphedDecoder``'s copy-back of each KDA
+    state (``graph_decode.py:262``) turns into a copy onto itself; only code
+    that keeps its own reference to an old state sees the difference.
     """
     import importlib
 
@@ -71,7 +92,9 @@ def install(kda_module=None, package=None):
     for mod in (kda_module, package):
         if mod is None:
             continue
-        for name, fn in (("kda_chunkwise", kda_chunkwise), ("kda_recurrent", kda_recurrent)):
+        chunk_fn, rec_fn = ((kda_chunkwise_inplace, kda_recurrent_inplace) if inplace_state
+                            else (kda_chunkwise, kda_recurrent))
+        for name, fn in (("kda_chunkwise", chunk_fn), ("kda_recurrent", rec_fn)):
             if hasattr(mod, name) and getattr(mod, name) is not fn:
                 _saved.append((mod, name, getattr(mod, name)))
                 setattr(mod, name, fn)

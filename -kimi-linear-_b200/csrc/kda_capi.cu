@@ -97,6 +97,13 @@ int validate(const KdaArgs* a, bool chunkwise) {
   if (a->state_in != nullptr &&
       reinterpret_cast<uintptr_t>(a->state_in) % (uintptr_t)elt_size(a->state_in_dtype))
     return KDA_ERR_ALIGNMENT;
+  // an output state that aliases the input (in-place update) must be exactly
+  // the same view: every kernel reads the state tile it owns before writing it
+  if (a->state_in != nullptr && a->state_in == a->state_out) {
+    if (a->state_in_dtype != a->state_out_dtype) return KDA_ERR_DTYPE;
+    for (int d = 0; d < 4; ++d)
+      if (a->state_in_stride[d] != a->state_out_stride[d]) return KDA_ERR_STRIDE;
+  }
   return KDA_OK;
 }
 

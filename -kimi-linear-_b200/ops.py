@@ -105,7 +105,7 @@ def _fill(args, q, k, v, g, beta, state_in, o, state_out, chunk_size):
     args.workspace_bytes = 0
 
 
-def _prepare(fn, q, k, v, g, beta, state, state_dtype):
+def _prepare(fn, q, k, v, g, beta, state, state_dtype, inplace=False):
     dev = _check_tensors(fn, [("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
                               ("state", state)])
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4 or g.dim() != 4 or beta.dim() != 3:
@@ -128,12 +128,21 @@ def _prepare(fn, q, k, v, g, beta, state, state_dtype):
     beta = _inner_contig(beta.float())        # kda.py:120,203
     if beta.numel() and beta.stride(-1) != 1:
         beta = beta.contiguous()
-    if state is not None:
-        state = _inner_contig(state)
     sdt = state_dtype or io
     if sdt not in _DT:
         raise TypeError(f"{fn}: unsupported state_dtype {sdt}")
     o = torch.empty(B, T, H, V, device=dev, dtype=io)
+    if inplace and state is not None:
+        # the new state overwrites `state` (every kernel reads the state tile it
+        # owns before writing it, so exact aliasing is safe)
+        if state.dtype != sdt:
+            raise TypeError(f"{fn}: inplace needs state.dtype == state_dtype or v.dtype "
+                            f"({state.dtype} vs {sdt})")
+        if state.stride(-1) != 1:
+            raise RuntimeError(f"{fn}: inplace needs a unit innermost state stride")
+        return dev, q, k, v, g, beta, state, o, state
+    if state is not None:
+        state = _inner_contig(state)
     S = torch.empty(B, H, K, V, device=dev, dtype=sdt)
     return dev, q, k, v, g, beta, state, o, S
 
@@ -150,13 +159,18 @@ def _call(fn_name, entry, args, dev):
 
 
 def kda_chunkwise(q, k, v, g, beta, initial_state=None, chunk_size=64, tile_size=0,
-                  state_dtype=None):
-    """Chunkwise KDA forward -- drop-in for ``kimi_linear/kda.py:58``."""
-    return chunkwise_impl(q, k, v, g, beta, initial_state, chunk_size, state_dtype)
+                  state_dtype=None, *, inplace=False):
+    """Chunkwise KDA forward -- drop-in for ``kimi_linear/kda.py:58``.
+
+    ``inplace=True`` (not in the reference; off by default) writes the final
+    state into ``initial_state`` and returns that tensor, instead of a new one
+    (the reference clones the state, ``kda.py:137``)."""
+    return chunkwise_impl(q, k, v, g, beta, initial_state, chunk_size, state_dtype,
+                          inplace=inplace)
 
 
 def chunkwise_impl(q, k, v, g, beta, initial_state=None, chunk_size=64, state_dtype=None,
-                   force_simt=False):
+                   force_simt=False, inplace=False):
     """``kda_chunkwise`` with an implementation switch: ``force_simt=True``
     runs the CUDA-core kernel even where the tcgen05 kernel applies (both
     are complete implementations; the switch exists to cross-check them)."""
@@ -169,9 +183,11 @@ def chunkwise_impl(q, k, v, g, beta, initial_state=None, chunk_size=64, state_dt
             f"kda_chunkwise: T={T} is not a multiple of chunk_size={C} "
             f"(the reference's reshape fails here too)")
     dev, q, k, v, g, beta, s0, o, S = _prepare("kda_chunkwise", q, k, v, g, beta,
-                                               initial_state, state_dtype)
+                                               initial_state, state_dtype, inplace)
     if o.numel() == 0 and S.numel() == 0:
         return o, S
+    if T == 0 and S is s0:
+        return o, S                                    # nothing to do, state unchanged
     lib = _lib.load()
     args = _lib.KdaArgs()
     _fill(args, q, k, v, g, beta, s0, o, S, C)
@@ -186,10 +202,15 @@ def chunkwise_impl(q, k, v, g, beta, initial_state=None, chunk_size=64, state_dt
     return o, S
 
 
-def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None):
-    """Token-recurrent KDA forward -- drop-in for ``kimi_linear/kda.py:188``."""
+def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None, *, inplace=False):
+    """Token-recurrent KDA forward -- drop-in for ``kimi_linear/kda.py:188``.
+
+    ``inplace=True`` (not in the reference; off by default) writes the new
+    state into ``state`` and returns that tensor: a decoder that keeps its
+    state in a static buffer (``GraphedDecoder``, ``graph_decode.py:262``) then
+    needs no copy-back -- its ``copy_`` becomes a copy onto itself."""
     dev, q, k, v, g, beta, s0, o, S = _prepare("kda_recurrent", q, k, v, g, beta,
-                                               state, state_dtype)
+                                               state, state_dtype, inplace)
     if o.numel() == 0 and S.numel() == 0:
         return o, S
     lib = _lib.load()

@@ -19,6 +19,10 @@
  * kda.py:119-120,202-203).  q is multiplied by `scale` inside the kernel (the
  * reference uses K^-0.5, kda.py:132,199).  Inputs are never written.
  *
+ * state_out may be exactly state_in (same pointer, dtype and strides) for an
+ * in-place state update: every kernel reads the state tile it owns before
+ * writing it.  Any other overlap between outputs and inputs is not allowed.
+ *
  * Every call is asynchronous on `stream` (a cudaStream_t, NULL = legacy
  * default stream), performs no host<->device synchronisation, no allocation
  * and no host read of device data, so it can be captured in a CUDA graph.

@@ -90,6 +90,14 @@ def test_validation_errors_without_device(lib):
     assert lib.kda_recurrent_fwd(ctypes.byref(_args(T=37, q=None)), None) == L.KDA_ERR_NULL_POINTER
     # B == 0: nothing to do, success without a device
     assert call(_args(B=0)) == L.KDA_OK
+    # an in-place state must be exactly the same view as the input state
+    alias = _args(state_in=1 << 21, state_out=1 << 21)
+    alias.state_in_dtype = L.DTYPE_F16
+    assert call(alias) == L.KDA_ERR_DTYPE
+    alias = _args(state_in=1 << 21, state_out=1 << 21)
+    alias.state_in_dtype = L.DTYPE_F32
+    alias.state_in_stride = (ctypes.c_int64 * 4)(4096, 1024, 64, 1)
+    assert call(alias) == L.KDA_ERR_STRIDE
 
 
 def test_path_selection_queries_need_no_device(lib):

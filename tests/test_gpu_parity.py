@@ -337,3 +337,68 @@ def test_bad_arguments_raise_on_gpu(cuda_dev):
     big = torch.zeros(1, 4, 1, 512, device=cuda_dev)
     with pytest.raises(RuntimeError, match="unsupported shape"):
         kb.kda_recurrent(big, big, big[..., :32], big, torch.zeros(1, 4, 1, device=cuda_dev))
+
+
+# --------------------------------------------------------------------------- #
+# in-place state update (opt-in, not in the reference)
+# --------------------------------------------------------------------------- #
+@pytest.mark.parametrize("which,shape,dtype", [
+    ("recurrent", (4, 1, 4, 128, 128), torch.float16),     # decode kernel
+    ("recurrent", (2, 5, 2, 64, 32), torch.float32),       # guarded kernel, T > 1
+    ("chunkwise", (1, 128, 2, 128, 128), torch.float16),   # tensor-core path
+    ("chunkwise", (2, 64, 2, 32, 32), torch.float32),      # CUDA-core path
+])
+def test_inplace_equals_out_of_place(which, shape, dtype, cuda_dev):
+    B, T, H, K, V = shape
+    kb = pkg()
+    x = kb.synth.make_inputs(B, T, H, K, V, dtype=dtype, seed=31, s0_std=0.02)
+    g = {n: t.to(cuda_dev) for n, t in x.items()}
+    args = [g[n] for n in ("q", "k", "v", "g", "beta")]
+    fn = kb.kda_recurrent if which == "recurrent" else kb.kda_chunkwise
+    kw = {} if which == "recurrent" else {"chunk_size": 64 if T % 64 == 0 else T}
+    st = g["S0"].clone()
+    o_ref, S_ref = fn(*args, st, state_dtype=torch.float32, **kw)
+    assert torch.equal(st, g["S0"])                           # default: input untouched
+    o_in, S_in = fn(*args, st, state_dtype=torch.float32, inplace=True, **kw)
+    assert S_in is st
+    assert torch.equal(S_in, S_ref) and torch.equal(o_in, o_ref)
+
+
+def test_graph_decode_inplace_needs_no_copy_back(cuda_dev):
+    """A captured single-token step that updates its static state in place
+    (no copy-back), replayed step after step, equals one eager call."""
+    kb = pkg()
+    B, H, K, V, steps = 8, 4, 128, 128, 24
+    x = kb.synth.make_inputs(B, steps, H, K, V, dtype=torch.float16, seed=33, s0_std=0.02)
+    x = {k: v.to(cuda_dev) for k, v in x.items()}
+    o_ref, S_ref = kb.kda_recurrent(x["q"], x["k"], x["v"], x["g"], x["beta"], state=x["S0"],
+                                    state_dtype=torch.float32)
+    state = x["S0"].clone()
+    tok = {n: x[n][:, :1].clone() for n in ("q", "k", "v", "g", "beta")}
+    out = torch.empty(B, 1, H, V, device=cuda_dev, dtype=torch.float16)
+
+    def step():
+        o, S = kb.kda_recurrent(tok["q"], tok["k"], tok["v"], tok["g"], tok["beta"],
+                                state=state, state_dtype=torch.float32, inplace=True)
+        out.copy_(o)
+
+    snap = state.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    state.copy_(snap)
+    outs = []
+    for t in range(steps):
+        for n in tok:
+            tok[n].copy_(x[n][:, t:t + 1])
+        graph.replay()
+        outs.append(out.clone())
+    torch.cuda.synchronize()
+    assert rel(torch.cat(outs, 1).float(), o_ref.float()) < 1e-5
+    assert rel(state, S_ref) < 1e-5
+    del graph

@@ -116,6 +116,19 @@ def test_reference_module_routes_through_patch():
         sys.path.remove(REF)
 
 
+def test_install_inplace_state_option():
+    kb = pkg()
+    pkg_mod, kda_mod, ref_chunk, ref_rec = _fake_reference()
+    kb.install(kda_module=kda_mod, package=pkg_mod, inplace_state=True)
+    try:
+        assert kda_mod.kda_chunkwise is kb.kda_chunkwise_inplace
+        assert kda_mod.kda_recurrent is kb.kda_recurrent_inplace
+        assert pkg_mod.kda_recurrent is kb.kda_recurrent_inplace
+    finally:
+        kb.uninstall()
+    assert kda_mod.kda_recurrent is ref_rec
+
+
 def test_install_module_patches_and_restores_methods():
     """install_module routes a KimiDeltaAttention-like class's _projections /
     _output through the fused drop-ins; uninstall_module restores them."""

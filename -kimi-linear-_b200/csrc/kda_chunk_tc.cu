@@ -155,11 +155,11 @@ constexpr int PREP_SMEM = P_TSLOT + 8;
 constexpr int kPrepTmemCols = 256;                     // D[128 x 256] fp32 of phase 5
 static_assert(P_A2 >= IMG_BYTES, "image staging");
 static_assert(PREP_SMEM <= 227 * 1024, "prep shared memory");
-// Aliases once their owners are dead: block decays Z[4][128] and exp(g_0)[128]
+// Aliases once their owners are dead: half-block decays Z[8][128] and exp(g_0)[128]
 // live in the L array during phase 1 (L is written only in phase 2, and only
 // where it is read later); M (fp32, pitch LMP) reuses the k*ra array and the
 // inversion scratch the q*ra array once the Gram is done.
-constexpr int PREP_THREADS = 256;
+constexpr int PREP_THREADS = 512;
 
 // 3xTF32 split: x ~= hi + lo with both parts exact in tf32
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
@@ -198,6 +198,26 @@ __device__ __forceinline__ void gemm16_3xtf32(float (*acc)[4], const float* Ab, 
   }
 }
 
+// C[16x8] += A[16 x 8*KSTEPS] * B[8*KSTEPS x 8] at ~fp32 accuracy (3xTF32),
+// one n-tile of gemm16_3xtf32: B(k, col) = Bb[k*ldb + col], col < 8
+template <int KSTEPS>
+__device__ __forceinline__ void gemm16x8_3xtf32(float* acc, const float* Ab, int lda,
+                                                const float* Bb, int ldb, int lane) {
+  const int gid = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    const int k0 = 8 * ks;
+    uint32_t ah[4], al[4], bh[2], bl[2];
+    split_tf32(Ab[gid * lda + k0 + tig], ah[0], al[0]);
+    split_tf32(Ab[(gid + 8) * lda + k0 + tig], ah[1], al[1]);
+    split_tf32(Ab[gid * lda + k0 + tig + 4], ah[2], al[2]);
+    split_tf32(Ab[(gid + 8) * lda + k0 + tig + 4], ah[3], al[3]);
+    split_tf32(Bb[(k0 + tig) * ldb + gid], bh[0], bl[0]);
+    split_tf32(Bb[(k0 + tig + 4) * ldb + gid], bh[1], bl[1]);
+    mma3_tf32(acc, ah, al, bh, bl);
+  }
+}
+
 // LOAD: how phase 1 reads its inputs -- 0 scalar loads, 1 two-element vector
 // loads, 2 vector loads and, every input row being a 16-byte-aligned range,
 // the next wave's L2 prefetch issued as one bulk (TMA-engine) prefetch per row.
@@ -212,8 +232,8 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   float* Axq = reinterpret_cast<float*>(sm + P_AXQ);
   float* Yb = reinterpret_cast<float*>(sm + P_YB);
   float* Lm = reinterpret_cast<float*>(sm + P_LM);
-  float* Zs = Lm;                  // [4][128] block decays (phase 1 only)
-  float* A0 = Lm + 4 * KD;         // [128]    exp(g of row 0) (phase 1 only)
+  float* Zs = Lm;                  // [4][2][128] half-block decay sums (phase 1 only)
+  float* A0 = Lm + 8 * KD;         // [128]       exp(g of row 0)        (phase 1 only)
   float* P02 = reinterpret_cast<float*>(sm + P_FAC);
   float* P03 = P02 + KD;
   float* P13 = P03 + KD;
@@ -260,7 +280,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       if constexpr (LOAD == 2) {                   // one TMA-engine prefetch per row
         const int c = tid >> 2, part = tid & 3;
         const int64_t t = (int64_t)n2 * CH + c;
-        if (t < p.T) {
+        if (c < CH && t < p.T) {
           if (part == 0)
             ptx::bulk_prefetch_l2(static_cast<const TIO*>(p.q) + b2 * p.q_s[0] + t * p.q_s[1] + h2 * p.q_s[2], KD * sizeof(TIO));
           else if (part == 1)
@@ -293,54 +313,64 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     }
   }
 
-  // ---- 1. per (16-row block r, channel pair): decays and decayed operands --
-  const int r = tid >> 6, k0 = 2 * (tid & 63);
+  // ---- 1. per (16-row block r, 8-row half hf, channel pair): decays and
+  // decayed operands.  Warp w: r = w / 4, hf = (w / 2) % 2, channels
+  // 64 (w % 2) .. +63 (a channel pair per lane).  The two halves of a block
+  // meet through shared memory (their partial decay sums).
+  const int r = warp >> 2, hf = (warp >> 1) & 1;
+  const int k0 = 64 * (warp & 1) + 2 * lane;
+  const int rb0 = 16 * r + 8 * hf;                 // first row of this thread
   // every input row of this thread, loaded unconditionally (rows past T are
-  // clamped to the last valid row and zeroed below) so the loads overlap
-  float2 gr[17], qr[16], kr[16], vr[16];
+  // clamped to the last valid row and zeroed below) so the loads overlap;
+  // gr[8] is the row after the half (next half or next block)
+  float2 gr[9], qr[8], kr[8], vr[8];
   {
 #pragma unroll
-    for (int i = 0; i < 17; ++i) {
-      const int c = min(16 * r + i, nvalid - 1);
+    for (int i = 0; i < 9; ++i) {
+      const int c = min(rb0 + i, nvalid - 1);
       gr[i] = ldg2<VEC>(gb + (int64_t)(t0 + c) * p.g_s[1] + k0);
     }
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int c = min(16 * r + i, nvalid - 1);
+    for (int i = 0; i < 8; ++i) {
+      const int c = min(rb0 + i, nvalid - 1);
       qr[i] = ldg2<VEC>(qb + (int64_t)(t0 + c) * p.q_s[1] + k0);
       kr[i] = ldg2<VEC>(kb + (int64_t)(t0 + c) * p.k_s[1] + k0);
       vr[i] = ldg2<VEC>(vb + (int64_t)(t0 + c) * p.v_s[1] + k0);
     }
   }
-  float2 al[17];                    // al[i] = exp(g) of row 16r + i (i >= 1)
-  float2 zr = make_float2(0.f, 0.f);
+  float2 al[9];                     // al[i] = exp(g) of row rb0 + i (i >= 1)
+  float2 zh = make_float2(0.f, 0.f);  // sum of g over rows rb0+1 .. rb0+8 (this half's share of Z_r)
 #pragma unroll
-  for (int i = 0; i < 17; ++i) {
-    const bool ok = (16 * r + i < nvalid) && !(i == 16 && r == 3);
+  for (int i = 0; i < 9; ++i) {
+    const bool ok = (rb0 + i < nvalid) && !(i == 8 && hf == 1 && r == 3);
     if (!ok) gr[i] = make_float2(0.f, 0.f);
     if (i >= 1) {
-      zr.x += gr[i].x;
-      zr.y += gr[i].y;
+      zh.x += gr[i].x;
+      zh.y += gr[i].y;
       al[i] = make_float2(__expf(gr[i].x), __expf(gr[i].y));
     }
   }
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    if (16 * r + i >= nvalid) qr[i] = kr[i] = vr[i] = make_float2(0.f, 0.f);
-  Zs[r * KD + k0] = zr.x;
-  Zs[r * KD + k0 + 1] = zr.y;
-  if (r == 0) {
+  for (int i = 0; i < 8; ++i)
+    if (rb0 + i >= nvalid) qr[i] = kr[i] = vr[i] = make_float2(0.f, 0.f);
+  Zs[(2 * r + hf) * KD + k0] = zh.x;                // [4 blocks][2 halves][128]
+  Zs[(2 * r + hf) * KD + k0 + 1] = zh.y;
+  if (r == 0 && hf == 0) {
     A0[k0] = expf(gr[0].x);
     A0[k0 + 1] = expf(gr[0].y);
   }
   __syncthreads();
   {
-    float eZx[4], eZy[4];
+    float Zx[4], Zy[4], eZx[4], eZy[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      eZx[j] = expf(Zs[j * KD + k0]);
-      eZy[j] = expf(Zs[j * KD + k0 + 1]);
+      Zx[j] = Zs[(2 * j) * KD + k0] + Zs[(2 * j + 1) * KD + k0];
+      Zy[j] = Zs[(2 * j) * KD + k0 + 1] + Zs[(2 * j + 1) * KD + k0 + 1];
+      eZx[j] = expf(Zx[j]);
+      eZy[j] = expf(Zy[j]);
     }
+    // the other half's share of the block decay
+    const float ox = Zs[(2 * r + (hf ^ 1)) * KD + k0], oy = Zs[(2 * r + (hf ^ 1)) * KD + k0 + 1];
     float bfx = A0[k0], bfy = A0[k0 + 1];        // exp(gc at the block start)
     float afx = 1.f, afy = 1.f;                  // exp(gc_last - gc at the next block start)
 #pragma unroll
@@ -348,7 +378,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       if (j < r) { bfx *= eZx[j]; bfy *= eZy[j]; }
       if (j > r) { afx *= eZx[j]; afy *= eZy[j]; }
     }
-    if (r == 0) {
+    if (r == 0 && hf == 0) {
       P02[k0] = eZx[1];                P02[k0 + 1] = eZy[1];
       P03[k0] = eZx[1] * eZx[2];       P03[k0 + 1] = eZy[1] * eZy[2];
       P13[k0] = eZx[2];                P13[k0 + 1] = eZy[2];
@@ -356,32 +386,35 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       dimg[k0] = A0[k0] * eZx[0] * eZx[1] * eZx[2] * eZx[3];
       dimg[k0 + 1] = A0[k0 + 1] * eZy[0] * eZy[1] * eZy[2] * eZy[3];
     }
-    {
-      const bool stx = zr.x < -kSteep, sty = zr.y < -kSteep;
-      Ef[r * KD + k0] = stx ? 0.f : expf(-zr.x);
-      Ef[r * KD + k0 + 1] = sty ? 0.f : expf(-zr.y);
+    if (hf == 0) {
+      const float zx = Zx[r], zy = Zy[r];
+      const bool stx = zx < -kSteep, sty = zy < -kSteep;
+      Ef[r * KD + k0] = stx ? 0.f : expf(-zx);
+      Ef[r * KD + k0 + 1] = sty ? 0.f : expf(-zy);
       const uint32_t bits = (stx ? 1u : 0u) | (sty ? 2u : 0u);
       if (bits) atomicOr(&steep[r * 4 + (k0 >> 5)], bits << (k0 & 31));
     }
-    // ra: prefix products from the block start; nb: suffix products to the next block start
-    float2 ra[16], nb[16];
-    if (r == 3) al[16] = make_float2(1.f, 1.f);
-    ra[0] = make_float2(1.f, 1.f);
+    // ra: prefix products from the block start (the second half starts from
+    // the first half's total); nb: suffix products to the next block start
+    // (the first half ends with the second half's total)
+    float2 ra[8], nb[8];
+    if (hf == 1 && r == 3) al[8] = make_float2(1.f, 1.f);
+    ra[0] = hf ? make_float2(__expf(ox), __expf(oy)) : make_float2(1.f, 1.f);
 #pragma unroll
-    for (int i = 1; i < 16; ++i) ra[i] = make_float2(ra[i - 1].x * al[i].x, ra[i - 1].y * al[i].y);
-    nb[15] = al[16];
+    for (int i = 1; i < 8; ++i) ra[i] = make_float2(ra[i - 1].x * al[i].x, ra[i - 1].y * al[i].y);
+    nb[7] = hf ? al[8] : make_float2(al[8].x * __expf(ox), al[8].y * __expf(oy));
 #pragma unroll
-    for (int i = 14; i >= 0; --i)
+    for (int i = 6; i >= 0; --i)
       nb[i] = make_float2(nb[i + 1].x * al[i + 1].x, nb[i + 1].y * al[i + 1].y);
-    // Qbar and Ktilde go out as 16-byte core-matrix rows: the four lanes of a
-    // quad hold the four channel pairs of one 8-channel group, so after a quad
-    // transpose of four rows each lane owns one whole row of the group.
+    // Qbar, Ktilde and V go out as 16-byte core-matrix rows: the four lanes of
+    // a quad hold the four channel pairs of one 8-channel group, so after a
+    // quad transpose of four rows each lane owns one whole row of the group.
 #pragma unroll
-    for (int i4 = 0; i4 < 16; i4 += 4) {
+    for (int i4 = 0; i4 < 8; i4 += 4) {
       uint32_t qh[4], kh[4], vh[4];
 #pragma unroll
       for (int ii = 0; ii < 4; ++ii) {
-        const int i = i4 + ii, c = 16 * r + i;
+        const int i = i4 + ii, c = rb0 + i;
         const float2 qv = qr[i], kv = kr[i], vv = vr[i];
         const float qsx = qv.x * s, qsy = qv.y * s;
         const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;   // exp(gc_c)
@@ -395,23 +428,21 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       quad_transpose(qh, tig);
       quad_transpose(kh, tig);
       quad_transpose(vh, tig);
-      const int c = 16 * r + i4 + tig;
+      const int c = rb0 + i4 + tig;
       *reinterpret_cast<uint4*>(img + IMG_U + vb_off(c, k0 & ~7)) = make_uint4(vh[0], vh[1], vh[2], vh[3]);
       *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(64 + c, k0 & ~7)) = make_uint4(qh[0], qh[1], qh[2], qh[3]);
       *reinterpret_cast<uint4*>(img + IMG_A1 + a1_off(c, k0 & ~7)) = make_uint4(kh[0], kh[1], kh[2], kh[3]);
     }
-    // Kbar^T (k rows, c cols): eight consecutive c of one channel per 16 bytes
-#pragma unroll
-    for (int i8 = 0; i8 < 16; i8 += 8) {
+    // Kbar^T (k rows, c cols): this thread's eight rows of one channel = 16 bytes
+    {
       uint32_t ex[4], ey[4];
 #pragma unroll
       for (int ii = 0; ii < 8; ii += 2) {
-        const int i = i8 + ii;
-        ex[ii / 2] = pack_h2(kr[i].x * nb[i].x * afx, kr[i + 1].x * nb[i + 1].x * afx);
-        ey[ii / 2] = pack_h2(kr[i].y * nb[i].y * afy, kr[i + 1].y * nb[i + 1].y * afy);
+        ex[ii / 2] = pack_h2(kr[ii].x * nb[ii].x * afx, kr[ii + 1].x * nb[ii + 1].x * afx);
+        ey[ii / 2] = pack_h2(kr[ii].y * nb[ii].y * afy, kr[ii + 1].y * nb[ii + 1].y * afy);
       }
-      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0, 16 * r + i8)) = make_uint4(ex[0], ex[1], ex[2], ex[3]);
-      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0 + 1, 16 * r + i8)) = make_uint4(ey[0], ey[1], ey[2], ey[3]);
+      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0, rb0)) = make_uint4(ex[0], ex[1], ex[2], ex[3]);
+      *reinterpret_cast<uint4*>(img + IMG_A3 + a2_off(k0 + 1, rb0)) = make_uint4(ey[0], ey[1], ey[2], ey[3]);
     }
   }
   ptx::fence_proxy_async_smem();
@@ -421,18 +452,18 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     ptx::bulk_commit();
   }
 
-  // ---- 2. Gram blocks: warp = (row block rr0, type); A fragments in registers.
-  // The K order inside each 16-channel group is permuted (sums are order-free)
-  // so every fragment element pair comes from one float4 load.  The 10 block
-  // pairs of a type are spread 2/2/3/3 over its four warps: row block 3 does
-  // j = 0..2 and the row-block-0 warp also takes block (3, 3).
+  // ---- 2. Gram blocks: 8 warps per type (L: x = k, Aout: x = s q); A
+  // fragments in registers.  The K order inside each 16-channel group is
+  // permuted (sums are order-free) so every fragment element pair comes from
+  // one float4 load.  The 10 block pairs (rr, j <= rr) of a type go one or
+  // two per warp: (3,0) (3,1) (3,2) (3,3) (2,0-1) (2,2) (1,0-1) (0,0).
   {
-    const int rr0 = warp & 3, type = warp >> 2;         // type 0: L (x = k), 1: Aout (x = s q)
+    const int type = warp >> 3, slot = warp & 7;
     const float* Ax = type ? Axq : Axk;
-#pragma unroll 1
-    for (int seg = 0; seg < (rr0 == 0 ? 2 : 1); ++seg) {
-    const int rr = seg ? 3 : rr0;
-    const int jlo = seg ? 3 : 0, jhi = seg ? 3 : (rr0 == 3 ? 2 : rr0);
+    const int rr = slot < 4 ? 3 : (slot < 6 ? 2 : (slot == 6 ? 1 : 0));
+    const int jlo = slot < 4 ? slot : (slot == 5 ? 2 : 0);
+    const int jhi = slot < 4 ? slot : (slot == 4 ? 1 : (slot == 5 ? 2 : (slot == 6 ? 1 : 0)));
+    {
     uint32_t af[8][2][4];                               // [16-channel group][k-step][frag]
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
@@ -554,37 +585,33 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       for (int c = 0; c < 16; ++c) Mm[(16 * rb + c) * LMP + 16 * rb + j] = x[c];
     }
   } else {
-    for (int idx = tid - 128; idx < CH * CH; idx += 128) {
+    for (int idx = tid - 128; idx < CH * CH; idx += PREP_THREADS - 128) {
       const int row = idx >> 6, col = idx & 63;
       if ((col >> 4) > (row >> 4)) Mm[row * LMP + col] = 0.f;
     }
   }
   __syncthreads();
-  // off-diagonal blocks M_rj = -D_r sum_{t=j}^{r-1} L_rt M_tj, by distance r - j
+  // off-diagonal blocks M_rj = -D_r sum_{t=j}^{r-1} L_rt M_tj, by distance r - j;
+  // a warp pair per block, one 8-column n-tile each (the products are
+  // column-separable)
   for (int dist = 1; dist <= 3; ++dist) {
-    if (warp < 4 - dist) {
-      const int j = warp, rb = warp + dist;
-      float tacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (warp < 2 * (4 - dist)) {
+      const int j = warp >> 1, nt = warp & 1, rb = j + dist;
+      float tacc[4] = {0.f, 0.f, 0.f, 0.f};
       const float* La = Lm + (16 * rb) * LMP + 16 * j;
-      const float* Mb = Mm + (16 * j) * LMP + 16 * j;
-      if (dist == 1) gemm16_3xtf32<2>(tacc, La, LMP, Mb, LMP, lane);
-      else if (dist == 2) gemm16_3xtf32<4>(tacc, La, LMP, Mb, LMP, lane);
-      else gemm16_3xtf32<6>(tacc, La, LMP, Mb, LMP, lane);
-      float* T = Ts + warp * (16 * TSP);
+      const float* Mb = Mm + (16 * j) * LMP + 16 * j + 8 * nt;
+      if (dist == 1) gemm16x8_3xtf32<2>(tacc, La, LMP, Mb, LMP, lane);
+      else if (dist == 2) gemm16x8_3xtf32<4>(tacc, La, LMP, Mb, LMP, lane);
+      else gemm16x8_3xtf32<6>(tacc, La, LMP, Mb, LMP, lane);
+      float* Tw = Ts + warp * (16 * TSP);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          T[(gid + 8 * (e >> 1)) * TSP + 8 * nt + 2 * tig + (e & 1)] = tacc[nt][e];
+      for (int e = 0; e < 4; ++e) Tw[(gid + 8 * (e >> 1)) * TSP + 2 * tig + (e & 1)] = tacc[e];
       __syncwarp();
-      float macc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      gemm16_3xtf32<2>(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, T, TSP, lane);
+      float macc[4] = {0.f, 0.f, 0.f, 0.f};
+      gemm16x8_3xtf32<2>(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, Tw, TSP, lane);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          Mm[(16 * rb + gid + 8 * (e >> 1)) * LMP + 16 * j + 8 * nt + 2 * tig + (e & 1)] =
-              -macc[nt][e];
+      for (int e = 0; e < 4; ++e)
+        Mm[(16 * rb + gid + 8 * (e >> 1)) * LMP + 16 * j + 8 * nt + 2 * tig + (e & 1)] = -macc[e];
     }
     __syncthreads();
   }
@@ -599,28 +626,24 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   // Aout M is block lower triangular like M: with it, one GEMM gives W, U,
   // Aout W = AM Ktilde and F = Aout U = AM V.
   {
-    const int rb = warp & 3, ch = warp >> 2;             // row block, 32-column half
+    const int rb = warp & 3, q4 = warp >> 2;             // row block, 16-column quarter
     const int mi = lane >> 3;
-    float acc[4][4] = {};
+    float acc[2][4] = {};
     for (int ks = 0; ks <= rb; ++ks) {
-      uint32_t a[4];
+      uint32_t a[4], bq[4];
       ptx::ldmatrix_x4(a, A2 + a2_off(64 + 16 * rb + (lane & 7) + ((mi & 1) ? 8 : 0),
                                       16 * ks + ((mi & 2) ? 8 : 0)));
-#pragma unroll
-      for (int nt = 0; nt < 4; nt += 2) {
-        uint32_t bq[4];
-        ptx::ldmatrix_x4_trans(bq, A2 + a2_off(16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0),
-                                               32 * ch + 8 * nt + ((mi & 2) ? 8 : 0)));
-        ptx::mma_f16_16x8x16(acc[nt], a, bq);
-        ptx::mma_f16_16x8x16(acc[nt + 1], a, bq + 2);
-      }
+      ptx::ldmatrix_x4_trans(bq, A2 + a2_off(16 * ks + (lane & 7) + ((mi & 1) ? 8 : 0),
+                                             16 * q4 + ((mi & 2) ? 8 : 0)));
+      ptx::mma_f16_16x8x16(acc[0], a, bq);
+      ptx::mma_f16_16x8x16(acc[1], a, bq + 2);
     }
     __syncthreads();                                     // every warp is done reading Aout
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr)
-        st_h2(A2, a2_off(64 + 16 * rb + gid + 8 * hr, 32 * ch + 8 * nt + 2 * tig),
+        st_h2(A2, a2_off(64 + 16 * rb + gid + 8 * hr, 16 * q4 + 8 * nt + 2 * tig),
               acc[nt][2 * hr], acc[nt][2 * hr + 1]);
   }
   ptx::fence_proxy_async_smem();                         // A2, Ktilde, V -> tensor core
@@ -664,11 +687,11 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   }
   {
     // TMEM lane quarter of this warp = D rows 32 lq .. 32 lq + 31 (one per lane);
-    // warps 0-3 read columns 0-127, warps 4-7 columns 128-255
-    const int lq = warp & 3, row = 32 * lq + lane, half = warp >> 2;
-    const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 128 * half;
+    // warp group qd = warp / 4 reads D columns 64 qd .. 64 qd + 63
+    const int lq = warp & 3, row = 32 * lq + lane, qd = warp >> 2, half = qd >> 1;
+    const uint32_t taddr = tbase + (static_cast<uint32_t>(32 * lq) << 16) + 64 * qd;
 #pragma unroll 1
-    for (int pc = 0; pc < 4; ++pc) {
+    for (int pc = 0; pc < 2; ++pc) {
       float v[32];
       ptx::tmem_ld<32>(taddr + 32 * pc, v);
       ptx::tmem_wait_ld();
@@ -677,7 +700,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
       // rows of one 8-column group are four (A1) or one (U, F) whole 128-byte
       // lines, so these 16-byte stores coalesce without staging
       for (int o = 0; o < 4; ++o) {
-        const int col = 32 * pc + 8 * o;
+        const int col = 64 * (qd & 1) + 32 * pc + 8 * o;    // within the 128-column half
         float* x = v + 8 * o;
         int off;
         if (half == 0) {

@@ -46,6 +46,9 @@ EXPORTED = (
     "kda_epilogue_fwd",
     "kda_prologue_args_size",
     "kda_epilogue_args_size",
+    "kda_backward",
+    "kda_backward_ckpt_floats",
+    "kda_backward_args_size",
     "kda_args_size",
     "kda_abi_version",
 )
@@ -131,6 +134,35 @@ class KdaEpilogueArgs(ctypes.Structure):
     ]
 
 
+class KdaBackwardArgs(ctypes.Structure):
+    """Mirror of ``struct KdaBackwardArgs``."""
+
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("B", ctypes.c_int32), ("T", ctypes.c_int32), ("H", ctypes.c_int32),
+        ("K", ctypes.c_int32), ("V", ctypes.c_int32),
+        ("io_dtype", ctypes.c_int32),
+        ("state_in_dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q", ctypes.c_void_p), ("q_stride", _I64x4),
+        ("k", ctypes.c_void_p), ("k_stride", _I64x4),
+        ("v", ctypes.c_void_p), ("v_stride", _I64x4),
+        ("g", ctypes.c_void_p), ("g_stride", _I64x4),
+        ("beta", ctypes.c_void_p), ("beta_stride", _I64x3),
+        ("state_in", ctypes.c_void_p), ("state_in_stride", _I64x4),
+        ("dout", ctypes.c_void_p), ("dout_stride", _I64x4),
+        ("dstate_out", ctypes.c_void_p), ("dstate_out_stride", _I64x4),
+        ("dq_part", ctypes.c_void_p),
+        ("dk_part", ctypes.c_void_p),
+        ("dg_part", ctypes.c_void_p),
+        ("dbeta_part", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p), ("dv_stride", _I64x4),
+        ("dstate_in", ctypes.c_void_p), ("dstate_in_stride", _I64x4),
+        ("ckpt", ctypes.c_void_p),
+        ("ckpt_floats", ctypes.c_size_t),
+    ]
+
+
 class KdaLibraryError(RuntimeError):
     """The CUDA library is missing or unusable (there is no fallback path)."""
 
@@ -161,6 +193,12 @@ def _declare(lib):
     lib.kda_prologue_fwd.restype = ctypes.c_int
     lib.kda_epilogue_fwd.argtypes = [ctypes.POINTER(KdaEpilogueArgs), ctypes.c_void_p]
     lib.kda_epilogue_fwd.restype = ctypes.c_int
+    lib.kda_backward.argtypes = [ctypes.POINTER(KdaBackwardArgs), ctypes.c_void_p]
+    lib.kda_backward.restype = ctypes.c_int
+    lib.kda_backward_ckpt_floats.argtypes = [ctypes.c_int] * 5
+    lib.kda_backward_ckpt_floats.restype = ctypes.c_size_t
+    lib.kda_backward_args_size.argtypes = []
+    lib.kda_backward_args_size.restype = ctypes.c_size_t
     lib.kda_prologue_args_size.argtypes = []
     lib.kda_prologue_args_size.restype = ctypes.c_size_t
     lib.kda_epilogue_args_size.argtypes = []
@@ -193,7 +231,8 @@ def load(path: str | None = None):
         if lib.kda_abi_version() != ABI_VERSION:
             raise KdaLibraryError(f"{p}: ABI version {lib.kda_abi_version()} != {ABI_VERSION}")
         for fn, st in (("kda_prologue_args_size", KdaPrologueArgs),
-                       ("kda_epilogue_args_size", KdaEpilogueArgs)):
+                       ("kda_epilogue_args_size", KdaEpilogueArgs),
+                       ("kda_backward_args_size", KdaBackwardArgs)):
             if getattr(lib, fn)() != ctypes.sizeof(st):
                 raise KdaLibraryError(f"{p}: {fn}() != ctypes sizeof {ctypes.sizeof(st)}")
         if lib.kda_args_size() != ctypes.sizeof(KdaArgs):

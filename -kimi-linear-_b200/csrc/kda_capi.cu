@@ -216,6 +216,52 @@ EpilogueParams to_epilogue(const KdaEpilogueArgs* a) {
   return p;
 }
 
+int validate_backward(const KdaBackwardArgs* a) {
+  if (a == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
+  if (a->B < 0 || a->T < 0 || a->H < 0) return KDA_ERR_SHAPE;
+  if (a->K != 32 && a->K != 64 && a->K != 128) return KDA_ERR_SHAPE;
+  if (a->V < 16 || a->V % 16 != 0) return KDA_ERR_SHAPE;
+  if (a->B > 65535 || a->H > 65535) return KDA_ERR_SHAPE;
+  if (!dtype_ok(a->io_dtype)) return KDA_ERR_DTYPE;
+  if (a->state_in != nullptr && !dtype_ok(a->state_in_dtype)) return KDA_ERR_DTYPE;
+  if (a->B == 0 || a->H == 0 || a->T == 0) return KDA_OK;
+  if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->dout || !a->dq_part || !a->dk_part ||
+      !a->dg_part || !a->dbeta_part || !a->dv || !a->ckpt)
+    return KDA_ERR_NULL_POINTER;
+  if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->g_stride[3] != 1 ||
+      a->dout_stride[3] != 1 || a->dv_stride[3] != 1)
+    return KDA_ERR_STRIDE;
+  if (a->state_in != nullptr && a->state_in_stride[3] != 1) return KDA_ERR_STRIDE;
+  if (a->dstate_out != nullptr && a->dstate_out_stride[3] != 1) return KDA_ERR_STRIDE;
+  if (a->dstate_in != nullptr && a->dstate_in_stride[3] != 1) return KDA_ERR_STRIDE;
+  if (a->ckpt_floats < backward_ckpt_floats(a->B, a->H, a->T, a->K, a->V)) return KDA_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(a->ckpt) % 16) return KDA_ERR_ALIGNMENT;
+  return KDA_OK;
+}
+
+BwdParams to_backward(const KdaBackwardArgs* a) {
+  BwdParams p{};
+  p.B = a->B; p.T = a->T; p.H = a->H; p.K = a->K; p.V = a->V;
+  p.io_dtype = a->io_dtype;
+  p.state_in_dtype = a->state_in ? a->state_in_dtype : KDA_DTYPE_F32;
+  p.scale = a->scale;
+  p.q = a->q; std::memcpy(p.q_s, a->q_stride, sizeof(p.q_s));
+  p.k = a->k; std::memcpy(p.k_s, a->k_stride, sizeof(p.k_s));
+  p.v = a->v; std::memcpy(p.v_s, a->v_stride, sizeof(p.v_s));
+  p.g = a->g; std::memcpy(p.g_s, a->g_stride, sizeof(p.g_s));
+  p.beta = a->beta; std::memcpy(p.b_s, a->beta_stride, sizeof(p.b_s));
+  p.state_in = a->state_in; std::memcpy(p.si_s, a->state_in_stride, sizeof(p.si_s));
+  p.dout = a->dout; std::memcpy(p.do_s, a->dout_stride, sizeof(p.do_s));
+  p.dstate_out = a->dstate_out; std::memcpy(p.dso_s, a->dstate_out_stride, sizeof(p.dso_s));
+  p.dq_part = a->dq_part; p.dk_part = a->dk_part; p.dg_part = a->dg_part;
+  p.dbeta_part = a->dbeta_part;
+  p.dv = a->dv; std::memcpy(p.dv_s, a->dv_stride, sizeof(p.dv_s));
+  p.dstate_in = a->dstate_in; std::memcpy(p.dsi_s, a->dstate_in_stride, sizeof(p.dsi_s));
+  p.ckpt = a->ckpt;
+  return p;
+}
+
 }  // namespace
 }  // namespace kda
 
@@ -310,6 +356,22 @@ int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream) {
   if (st != KDA_OK) return st;
   return launch_status(launch_epilogue(to_epilogue(args), static_cast<cudaStream_t>(stream)));
 }
+
+int kda_backward(const KdaBackwardArgs* args, void* stream) {
+  int st = validate_backward(args);
+  if (st != KDA_OK) return st;
+  if (args->B == 0 || args->H == 0 || args->T == 0) return KDA_OK;
+  st = check_arch();
+  if (st != KDA_OK) return st;
+  return launch_status(launch_backward(to_backward(args), static_cast<cudaStream_t>(stream)));
+}
+
+size_t kda_backward_ckpt_floats(int B, int H, int T, int K, int V) {
+  if (B < 0 || H < 0 || T < 0 || K < 0 || V < 0) return 0;
+  return backward_ckpt_floats(B, H, T, K, V);
+}
+
+size_t kda_backward_args_size(void) { return sizeof(KdaBackwardArgs); }
 
 size_t kda_prologue_args_size(void) { return sizeof(KdaPrologueArgs); }
 

@@ -64,6 +64,27 @@ struct EpilogueParams {
   void* y; int64_t y_s[2];
 };
 
+// Device-side view of KdaBackwardArgs.
+struct BwdParams {
+  int B, T, H, K, V, io_dtype, state_in_dtype;
+  float scale;
+  const void* q; int64_t q_s[4];
+  const void* k; int64_t k_s[4];
+  const void* v; int64_t v_s[4];
+  const float* g; int64_t g_s[4];
+  const float* beta; int64_t b_s[3];
+  const void* state_in; int64_t si_s[4];
+  const void* dout; int64_t do_s[4];
+  const float* dstate_out; int64_t dso_s[4];
+  float *dq_part, *dk_part, *dg_part, *dbeta_part;
+  float* dv; int64_t dv_s[4];
+  float* dstate_in; int64_t dsi_s[4];
+  float* ckpt;
+};
+
+size_t backward_ckpt_floats(int B, int H, int T, int K, int V);
+cudaError_t launch_backward(const BwdParams& p, cudaStream_t s);
+
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t s);
 cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s);
 

@@ -19,9 +19,19 @@
 Everything runs on the current CUDA stream of the inputs' device: no host
 synchronisation, no host reads of device values, outputs from PyTorch's
 caching allocator -- so the calls can be captured in a CUDA graph
-(``kimi_linear/graph_decode.py:269-289``).  The kernels are forward-only: a
-call that would need gradients raises instead of returning values autograd
-cannot differentiate.  There is no CPU path: CPU tensors raise.
+(``kimi_linear/graph_decode.py:269-289``).  There is no CPU path: CPU tensors
+raise.
+
+Gradients: the reference's trainers differentiate through both functions with
+torch autograd.  When grad mode is on and an input requires grad, the call
+runs the same forward kernel inside :class:`_KdaFunction`, whose backward is
+the ``kda_backward`` kernel -- the exact reverse-mode gradient of the token
+recurrence that both functions compute (``kda.py:207-216``).  It supports
+K in {32, 64, 128} and V % 16 == 0 and raises otherwise.  One deliberate
+difference: for fp16 outputs ``kda_recurrent`` clamps ``o`` to the fp16 range
+(``kda.py:217-218``) and autograd zeroes the gradient of clamped entries; the
+kernel passes every entry's gradient through (the two differ only where the
+output overflowed fp16).
 """
 
 from __future__ import annotations
@@ -165,6 +175,11 @@ def kda_chunkwise(q, k, v, g, beta, initial_state=None, chunk_size=64, tile_size
     ``inplace=True`` (not in the reference; off by default) writes the final
     state into ``initial_state`` and returns that tensor, instead of a new one
     (the reference clones the state, ``kda.py:137``)."""
+    if _needs_grad(q, k, v, g, beta, initial_state):
+        if inplace:
+            raise RuntimeError("kda_chunkwise: inplace=True cannot record gradients")
+        return _with_grad("kda_chunkwise", q, k, v, g, beta, initial_state,
+                          lambda *t: chunkwise_impl(*t, chunk_size, state_dtype))
     return chunkwise_impl(q, k, v, g, beta, initial_state, chunk_size, state_dtype,
                           inplace=inplace)
 
@@ -209,6 +224,11 @@ def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None, *, inplace=Fal
     state into ``state`` and returns that tensor: a decoder that keeps its
     state in a static buffer (``GraphedDecoder``, ``graph_decode.py:262``) then
     needs no copy-back -- its ``copy_`` becomes a copy onto itself."""
+    if _needs_grad(q, k, v, g, beta, state):
+        if inplace:
+            raise RuntimeError("kda_recurrent: inplace=True cannot record gradients")
+        return _with_grad("kda_recurrent", q, k, v, g, beta, state,
+                          lambda *t: kda_recurrent(*t, state_dtype))
     dev, q, k, v, g, beta, s0, o, S = _prepare("kda_recurrent", q, k, v, g, beta,
                                                state, state_dtype, inplace)
     if o.numel() == 0 and S.numel() == 0:
@@ -218,6 +238,125 @@ def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None, *, inplace=Fal
     _fill(args, q, k, v, g, beta, s0, o, S, 1)
     _call("kda_recurrent", lib.kda_recurrent_fwd, args, dev)
     return o, S
+
+
+def _needs_grad(*ts):
+    return torch.is_grad_enabled() and any(
+        isinstance(t, torch.Tensor) and t.requires_grad for t in ts)
+
+
+class _KdaFunction(torch.autograd.Function):
+    """Forward: one of the forward kernels (``run``); backward: ``kda_backward``.
+
+    Inputs arrive in the dtypes the kernels read (q, k in v's dtype; g, beta
+    fp32); the conversions before :meth:`apply` are ordinary differentiable
+    torch ops, so autograd casts each gradient back to the caller's dtype."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, state, run):
+        o, S = run(q, k, v, g, beta, state)
+        ctx.save_for_backward(q, k, v, g, beta, state)
+        ctx.set_materialize_grads(False)
+        return o, S
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, do, dS):
+        q, k, v, g, beta, state = ctx.saved_tensors
+        grads = kda_backward(q, k, v, g, beta, state, do, dS)
+        need = ctx.needs_input_grad
+        out = [gr if need[i] else None for i, gr in enumerate(grads)]
+        return (*out, None)
+
+
+def kda_backward(q, k, v, g, beta, state, do, dS):
+    """Gradients ``(dq, dk, dv, dg, dbeta, dstate)`` of the KDA forward
+    ``(o, S) = f(q, k, v, g, beta, state)`` for output gradients ``do``
+    (of ``o``, or None) and ``dS`` (of the returned state, or None).
+
+    ``q``, ``k``, ``v`` share one dtype; ``g``, ``beta`` fp32; ``state`` is
+    None (zero initial state, ``dstate`` None) or [B, H, K, V] in any
+    supported dtype.  dq, dk, dv come back in v's dtype, dg and dbeta fp32,
+    dstate in ``state``'s dtype.  Reduction over V tiles: the kernel writes
+    per-16-column partial sums of dq, dk, dg and dbeta, summed here."""
+    fn = "kda_backward"
+    dev = _check_tensors(fn, [("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
+                              ("state", state), ("do", do), ("dS", dS)])
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    io = v.dtype
+    if q.dtype != io or k.dtype != io or g.dtype != torch.float32 or \
+            beta.dtype != torch.float32:
+        raise TypeError(f"{fn}: q, k, v must share one dtype and g, beta be fp32")
+    q, k, v, g = (_inner_contig(t) for t in (q, k, v, g))
+    beta = beta if beta.numel() == 0 or beta.stride(-1) == 1 else beta.contiguous()
+    if state is not None:
+        state = _inner_contig(state)
+    if do is None:
+        do = torch.zeros(B, T, H, V, device=dev, dtype=io)
+    else:
+        do = _inner_contig(do.to(io))
+    if dS is not None:
+        dS = _inner_contig(dS.float())
+    dv = torch.empty(B, T, H, V, device=dev, dtype=torch.float32)
+    dstate = (torch.empty(B, H, K, V, device=dev, dtype=torch.float32)
+              if state is not None else None)
+    nvt = max(V // 16, 1)
+    dq_p = torch.empty(nvt, B, T, H, K, device=dev, dtype=torch.float32)
+    dk_p = torch.empty_like(dq_p)
+    dg_p = torch.empty_like(dq_p)
+    db_p = torch.empty(nvt, B, T, H, device=dev, dtype=torch.float32)
+    if B * T * H == 0:
+        if dstate is not None:
+            dstate.copy_(dS if dS is not None else torch.zeros_like(dstate))
+        z = dq_p.sum(0)
+        return (z.to(io), z.to(io), dv.zero_().to(io), z, db_p.sum(0),
+                None if state is None else dstate.to(state.dtype))
+    lib = _lib.load()
+    ck_n = int(lib.kda_backward_ckpt_floats(B, H, T, K, V))
+    ckpt = torch.empty(max(ck_n, 4), device=dev, dtype=torch.float32)
+    a = _lib.KdaBackwardArgs()
+    a.abi_version = _lib.ABI_VERSION
+    a.B, a.T, a.H, a.K, a.V = B, T, H, K, V
+    a.io_dtype = _DT[io]
+    a.scale = float(K) ** -0.5
+    a.q, a.q_stride = q.data_ptr(), _strides(q, 4)
+    a.k, a.k_stride = k.data_ptr(), _strides(k, 4)
+    a.v, a.v_stride = v.data_ptr(), _strides(v, 4)
+    a.g, a.g_stride = g.data_ptr(), _strides(g, 4)
+    a.beta, a.beta_stride = beta.data_ptr(), _strides(beta, 3)
+    if state is not None:
+        a.state_in, a.state_in_stride = state.data_ptr(), _strides(state, 4)
+        a.state_in_dtype = _DT[state.dtype]
+        a.dstate_in, a.dstate_in_stride = dstate.data_ptr(), _strides(dstate, 4)
+    else:
+        a.state_in_dtype = _lib.DTYPE_F32
+    a.dout, a.dout_stride = do.data_ptr(), _strides(do, 4)
+    if dS is not None:
+        a.dstate_out, a.dstate_out_stride = dS.data_ptr(), _strides(dS, 4)
+    a.dq_part, a.dk_part = dq_p.data_ptr(), dk_p.data_ptr()
+    a.dg_part, a.dbeta_part = dg_p.data_ptr(), db_p.data_ptr()
+    a.dv, a.dv_stride = dv.data_ptr(), _strides(dv, 4)
+    a.ckpt, a.ckpt_floats = ckpt.data_ptr(), ck_n
+    _call(fn, lib.kda_backward, a, dev)
+    dq, dk, dg, db = dq_p.sum(0), dk_p.sum(0), dg_p.sum(0), db_p.sum(0)
+    return (dq.to(io), dk.to(io), dv.to(io), dg, db,
+            None if state is None else dstate.to(state.dtype))
+
+
+def _with_grad(fn, q, k, v, g, beta, state, run):
+    """Route a call that needs gradients through :class:`_KdaFunction`."""
+    _check_grad_inputs(fn, q, k, v, g, beta, state)
+    io = v.dtype
+    q = q if q.dtype == io else q.to(io)
+    k = k if k.dtype == io else k.to(io)
+    return _KdaFunction.apply(q, k, v, g.float(), beta.float(), state, run)
+
+
+def _check_grad_inputs(fn, q, k, v, g, beta, state):
+    with torch.no_grad():
+        _check_tensors(fn, [("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
+                            ("state", state)])
 
 
 def device_error(clear=True):

@@ -223,6 +223,55 @@ typedef struct KdaEpilogueArgs {
 
 int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream);
 
+/*
+ * Gradient of the KDA forward (kda_chunkwise or kda_recurrent: the same
+ * function) with respect to q, k, v, g, beta and the initial state, given the
+ * gradients of o and of the returned state.  The reference obtains it from
+ * torch autograd through kimi_linear/kda.py:58-219; this is the exact
+ * reverse-mode gradient of the token recurrence (kda.py:207-216).
+ *
+ *   dout       : [B, T, H, V] in io_dtype (gradient of o)
+ *   dstate_out : [B, H, K, V] fp32 (gradient of the returned state) or NULL
+ *   dv         : [B, T, H, V] fp32 output
+ *   dstate_in  : [B, H, K, V] fp32 output, or NULL
+ *   dq_part, dk_part, dg_part : [V/16, B, T, H, K] fp32 partial sums over
+ *                16-column tiles of V (dq, dk, dg = their sums over axis 0)
+ *   dbeta_part : [V/16, B, T, H] fp32 partial sums
+ *   ckpt       : workspace of kda_backward_ckpt_floats() fp32 values
+ * Requires K in {32, 64, 128} and V % 16 == 0.
+ */
+typedef struct KdaBackwardArgs {
+  int32_t abi_version;
+  int32_t B, T, H, K, V;
+  int32_t io_dtype;
+  int32_t state_in_dtype;
+  float scale;
+  const void* q;     int64_t q_stride[4];
+  const void* k;     int64_t k_stride[4];
+  const void* v;     int64_t v_stride[4];
+  const float* g;    int64_t g_stride[4];
+  const float* beta; int64_t beta_stride[3];
+  const void* state_in;  int64_t state_in_stride[4];   /* NULL = zero state */
+  const void* dout;      int64_t dout_stride[4];
+  const float* dstate_out; int64_t dstate_out_stride[4];
+  float* dq_part;
+  float* dk_part;
+  float* dg_part;
+  float* dbeta_part;
+  float* dv;         int64_t dv_stride[4];
+  float* dstate_in;  int64_t dstate_in_stride[4];
+  float* ckpt;
+  size_t ckpt_floats;
+} KdaBackwardArgs;
+
+int kda_backward(const KdaBackwardArgs* args, void* stream);
+
+/* fp32 values of the backward checkpoint workspace: B * H * ceil(T/64) * K * V. */
+size_t kda_backward_ckpt_floats(int B, int H, int T, int K, int V);
+
+/* sizeof(KdaBackwardArgs) as compiled. */
+size_t kda_backward_args_size(void);
+
 /* sizeof(KdaPrologueArgs) / sizeof(KdaEpilogueArgs) as compiled. */
 size_t kda_prologue_args_size(void);
 size_t kda_epilogue_args_size(void);

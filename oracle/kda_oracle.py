@@ -250,6 +250,72 @@ def kda_recurrent(q, k, v, g, beta, state=None, state_dtype=None, v_dtype=None):
 
 
 # --------------------------------------------------------------------------- #
+# gradient of kda_recurrent / kda_chunkwise (torch autograd in the reference)
+# --------------------------------------------------------------------------- #
+def kda_backward(q, k, v, g, beta, state=None, do=None, dS=None):
+    """Reverse-mode gradient of the token recurrence ``kda.py:207-216``, float64.
+
+    The reference's trainers get these gradients from torch autograd through
+    ``kda_recurrent`` (``kda.py:188-219``) or ``kda_chunkwise`` (``kda.py:58-185``,
+    the same function).  This restates the chain rule of one step backwards::
+
+        St = Diag(a) S_{t-1}, x = k^T St, u = beta (v - x), S_t = St + k u^T,
+        o = S_t^T q'                         (a = exp g, q' = K^-0.5 q)
+
+        dS += q' do^T;  dq' = S_t do;  du = dS^T k;  dv = beta du;
+        dbeta = du . (v - x);  dx = -beta du;  dk = dS u + St dx;
+        dSt = dS + k dx^T;  dg = rowsum(dSt (.) St);  dS_{t-1} = Diag(a) dSt
+
+    ``do`` [B,T,H,V] / ``dS`` [B,H,K,V] may be None (zero).  Returns float64
+    ``(dq, dk, dv, dg, dbeta, dstate)``; ``dstate`` is None without ``state``.
+    Inputs are read as float32 values, like the reference (``kda.py:199-203``).
+    The fp16 output clamp (``kda.py:217-218``) is not differentiated through.
+    """
+    f = np.float64
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    sc = f(_F32(K ** -0.5))
+    qs = np.asarray(q, dtype=_F32).astype(f) * sc
+    k64 = np.asarray(k, dtype=_F32).astype(f)
+    v64 = np.asarray(v, dtype=_F32).astype(f)
+    al = np.exp(np.asarray(g, dtype=_F32).astype(f))
+    b64 = np.asarray(beta, dtype=_F32).astype(f)
+    do64 = (np.zeros((B, T, H, V)) if do is None
+            else np.asarray(do, dtype=_F32).astype(f))
+    S = (np.zeros((B, H, K, V)) if state is None
+         else np.asarray(state, dtype=_F32).astype(f))
+    prev, us, xs = [], [], []
+    for t in range(T):                         # forward, keeping S_{t-1}, u, v - x
+        prev.append(S)
+        St = S * al[:, t][..., None]
+        x = np.einsum("bhk,bhkv->bhv", k64[:, t], St)
+        vmx = v64[:, t] - x
+        u = b64[:, t][..., None] * vmx
+        S = St + k64[:, t][..., None] * u[..., None, :]
+        us.append(u)
+        xs.append(vmx)
+    dq = np.zeros((B, T, H, K)); dk = np.zeros((B, T, H, K)); dg = np.zeros((B, T, H, K))
+    dv = np.zeros((B, T, H, V)); db = np.zeros((B, T, H))
+    dSt_acc = np.zeros((B, H, K, V)) if dS is None else np.asarray(dS, dtype=_F32).astype(f)
+    for t in range(T - 1, -1, -1):
+        kt, at, bt = k64[:, t], al[:, t], b64[:, t]
+        St = prev[t] * at[..., None]
+        Snew = St + kt[..., None] * us[t][..., None, :]
+        dSt_acc = dSt_acc + qs[:, t][..., None] * do64[:, t][..., None, :]
+        dq[:, t] = np.einsum("bhkv,bhv->bhk", Snew, do64[:, t]) * sc
+        du = np.einsum("bhkv,bhk->bhv", dSt_acc, kt)
+        dv[:, t] = bt[..., None] * du
+        db[:, t] = np.einsum("bhv,bhv->bh", du, xs[t])
+        dx = -bt[..., None] * du
+        dk[:, t] = (np.einsum("bhkv,bhv->bhk", dSt_acc, us[t])
+                    + np.einsum("bhkv,bhv->bhk", St, dx))
+        dSt = dSt_acc + kt[..., None] * dx[..., None, :]
+        dg[:, t] = np.einsum("bhkv,bhkv->bhk", dSt, St)
+        dSt_acc = dSt * at[..., None]
+    return dq, dk, dv, dg, db, (None if state is None else dSt_acc)
+
+
+# --------------------------------------------------------------------------- #
 # comparison metric
 # --------------------------------------------------------------------------- #
 def rel_err(a, b) -> float:

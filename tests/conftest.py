@@ -33,7 +33,24 @@ def pkg():
 def golden_cases():
     """Golden cases of the KDA core (tests/golden/make_golden.py)."""
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                  if not os.path.basename(p).startswith("fused_"))
+                  if not os.path.basename(p).startswith(("fused_", "grad_")))
+
+
+def grad_cases():
+    """Golden gradient cases (tests/golden/make_golden_grad.py)."""
+    return sorted(os.path.basename(p)[:-4]
+                  for p in glob.glob(os.path.join(GOLDEN, "grad_*.npz")))
+
+
+def load_grad(name):
+    """Golden gradient case ``name``: dict of numpy arrays plus ``fn``, ``dtype``,
+    ``state_dtype`` (strings) and B, T, H, K, V, C."""
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    d = {k: z[k] for k in z.files}
+    B, T, H, K, V, C = (int(x) for x in d["meta"])
+    d.update(B=B, T=T, H=H, K=K, V=V, C=None if C < 0 else C, fn=str(d["fn"]),
+             dtype=str(d["dtype"]), state_dtype=str(d["state_dtype"]) or None)
+    return d
 
 
 def fused_cases():

@@ -1,5 +1,5 @@
 """Host-side behaviour of the reference-signature shim (no GPU needed):
-argument checking, the forward-only guard, the absence of any CPU path, and
+argument checking, the gradient path, the absence of any CPU path, and
 ``install()`` patching the reference's module globals."""
 
 from __future__ import annotations
@@ -36,11 +36,27 @@ def test_ragged_t_raises_like_reference():
         pkg().kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=0)
 
 
-def test_forward_only_guard():
+def test_grad_path_has_no_cpu_fallback():
+    """Inputs that require grad take the autograd path; it too needs CUDA."""
     x = _inputs()
     q = x["q"].clone().requires_grad_(True)
-    with pytest.raises(RuntimeError):
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
         pkg().kda_recurrent(q, x["k"], x["v"], x["g"], x["beta"])
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        pkg().kda_chunkwise(q, x["k"], x["v"], x["g"], x["beta"], chunk_size=64)
+    with pytest.raises(RuntimeError, match="cannot record gradients"):
+        pkg().kda_recurrent(q, x["k"], x["v"], x["g"], x["beta"], state=x["S0"],
+                            inplace=True)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        pkg().ops.kda_backward(x["q"], x["k"], x["v"], x["g"], x["beta"], None,
+                               x["v"], None)
+
+
+def test_fused_kernels_stay_forward_only():
+    kb = pkg()
+    t = torch.zeros(1, 4, 64, requires_grad=True)
+    with pytest.raises(RuntimeError):
+        kb.kda_epilogue(t.view(1, 4, 1, 64), t, torch.ones(1, 64), 1e-6)
 
 
 def test_package_alias_registered():

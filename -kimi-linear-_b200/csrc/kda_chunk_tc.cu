@@ -747,7 +747,10 @@ struct StateCfg {
   static constexpr int ST_U = 50176;                           // shared part, 1 KiB padded
   static constexpr int ST_F = ST_U + SLICE;
   static constexpr int STAGE = ((ST_F + SLICE + 1023) / 1024) * 1024;
-  static constexpr int SB_OFF = 2 * STAGE;                     // S  (K = 128) f16
+  // chunk images in flight: three where they fit (the refill of a stage is
+  // issued when its chunk is done, so with three it has two chunk periods to land)
+  static constexpr int NST = 3 * STAGE + (KD + CH) * VS * 2 + 64 <= 227 * 1024 ? 3 : 2;
+  static constexpr int SB_OFF = NST * STAGE;                   // S  (K = 128) f16
   static constexpr int PB_OFF = SB_OFF + KD * VS * 2;          // P  (K = 64)  f16
   static constexpr int BAR_OFF = PB_OFF + CH * VS * 2;
   static constexpr int SMEM = BAR_OFF + 64;
@@ -800,11 +803,12 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* Sb = sm + Cfg::SB_OFF;
   uint8_t* Pb = sm + Cfg::PB_OFF;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [2] chunk images
-  uint64_t* mbarA = full + 2;      // R1 = [-W; E] S done           (one phase per chunk)
-  uint64_t* mbarB = full + 3;      // R3 += Kbar^T P done           (one phase per chunk)
-  uint64_t* fcons = full + 4;      // warps 2-3 finished reading F  (one phase per chunk)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + 5);
+  constexpr int NST = Cfg::NST;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [NST] chunk images
+  uint64_t* mbarA = full + NST;        // R1 = [-W; E] S done           (one phase per chunk)
+  uint64_t* mbarB = full + NST + 1;    // R3 += Kbar^T P done           (one phase per chunk)
+  uint64_t* fcons = full + NST + 2;    // warps 2-3 finished reading F  (one phase per chunk)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(full + NST + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -819,8 +823,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     ptx::tmem_relinquish();
   }
   if (tid == 0) {
-    ptx::mbar_init(&full[0], 1);
-    ptx::mbar_init(&full[1], 1);
+    for (int sg = 0; sg < NST; ++sg) ptx::mbar_init(&full[sg], 1);
     ptx::mbar_init(mbarA, 1);
     ptx::mbar_init(mbarB, 1);
     ptx::mbar_init(fcons, 64);
@@ -836,7 +839,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   // thread 64 (the copy issuer): stages with a bulk copy in flight and their phase parity
   uint32_t pending = 0, pend_par = 0;
   if (tid == 64) {
-    for (int sg = 0; sg < 2 && sg < NT; ++sg) {
+    for (int sg = 0; sg < NST && sg < NT; ++sg) {
       fetch_chunk<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
       pending |= 1u << sg;
     }
@@ -856,21 +859,19 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   }
   ptx::tmem_wait_st();
 
-  // shared-memory descriptors of every operand, both stages (built once);
-  // they advance by 256 bytes (16 in the >>4 address field) per k-step
-  const uint32_t st0 = ptx::smem_u32(sm), st1 = ptx::smem_u32(sm + Cfg::STAGE);
-  const uint64_t dA1_0 = ptx::sdesc(st0 + IMG_A1, 128, 2048), dA1_1 = ptx::sdesc(st1 + IMG_A1, 128, 2048);
-  const uint64_t dA3_0 = ptx::sdesc(st0 + IMG_A3, 128, 1024), dA3_1 = ptx::sdesc(st1 + IMG_A3, 128, 1024);
+  // shared-memory descriptors of the fixed operands (built once); all
+  // descriptors advance by 256 bytes (16 in the >>4 address field) per k-step
+  const uint32_t st0 = ptx::smem_u32(sm);
   const uint64_t dSb = ptx::sdesc(ptx::smem_u32(Sb), 128, 2048);
   const uint64_t dPb = ptx::sdesc(ptx::smem_u32(Pb), 128, 1024);
 
   bool aborted = false;
   for (int n = 0; n < NT; ++n) {
-    const int sg = n & 1;
+    const int sg = n % NST;
     uint8_t* stg = sm + sg * Cfg::STAGE;
     const uint32_t par = static_cast<uint32_t>(n & 1);
     // every thread waits for image n itself (bounded)
-    if (ptx::mbar_wait(&full[sg], (n >> 1) & 1, kWaitNs)) {
+    if (ptx::mbar_wait(&full[sg], (n / NST) & 1, kWaitNs)) {
       if (tid == 64) pending &= ~(1u << sg);
     } else {
       *abort_flag = 1;
@@ -900,7 +901,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     if (*abort_flag) { aborted = true; break; }
     if (warp == 0) {                                       // warp-uniform issue, one lane
       ptx::tc_fence_after();
-      const uint64_t dA1 = sg ? dA1_1 : dA1_0;
+      const uint64_t dA1 = ptx::sdesc(st0 + sg * Cfg::STAGE + IMG_A1, 128, 2048);
       if (ptx::elect_one()) {
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)                     // R1 = [-W; E] S
@@ -933,7 +934,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
       named_barrier_64();                                  // P ready (warps 0-1)
       if (warp == 0) {
         ptx::tc_fence_after();
-        const uint64_t dA3 = sg ? dA3_1 : dA3_0;
+        const uint64_t dA3 = ptx::sdesc(st0 + sg * Cfg::STAGE + IMG_A3, 128, 1024);
         if (ptx::elect_one()) {
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)                   // R3 += Kbar^T P
@@ -976,12 +977,12 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
     ptx::tc_fence_after();
     // thread 64 refills the stage (off the chain that warp 0 runs): after the
     // second batch the MMAs and warps 0-1 are done with it, after fcons warps 2-3
-    if (tid == 64 && n + 2 < NT && !*abort_flag) {         // stage free: fetch chunk n+2
+    if (tid == 64 && n + NST < NT && !*abort_flag) {       // stage free: fetch chunk n+NST
       if (ptx::mbar_wait(fcons, par, kWaitNs)) {
         ptx::fence_proxy_async_smem();
-        fetch_chunk<VS>(stg, wsh + (size_t)(n + 2) * IMG_BYTES, v0, &full[sg]);
+        fetch_chunk<VS>(stg, wsh + (size_t)(n + NST) * IMG_BYTES, v0, &full[sg]);
         pending |= 1u << sg;
-        pend_par = (pend_par & ~(1u << sg)) | ((((n + 2) >> 1) & 1u) << sg);
+        pend_par = (pend_par & ~(1u << sg)) | ((((n + NST) / NST) & 1u) << sg);
       } else {
         *abort_flag = 1;
       }
@@ -1005,7 +1006,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   } else if (tid == 64) {
     atomicExch(&g_kda_device_error, 1);
     // let bulk copies still in flight land before this CTA's smem is released
-    for (int sg = 0; sg < 2; ++sg)
+    for (int sg = 0; sg < NST; ++sg)
       if (pending & (1u << sg)) ptx::mbar_wait(&full[sg], (pend_par >> sg) & 1u, kWaitNs / 2);
   }
   ptx::tc_fence_before();
@@ -1013,6 +1014,273 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   if (warp == 0) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tbase, Cfg::NCOL);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// state kernel, register-resident variant
+// ---------------------------------------------------------------------------
+// The same chain as state_kernel, S' = d (.) S + Kbar^T (U - W S) and
+// O = E S + F per chunk, with the fp32 master state held in mma.sync
+// accumulator registers: S' accumulates Kbar^T P straight onto d (.) S, and the
+// only hand-offs per chunk are the f16 copies of S and P through shared memory.
+// The chain is latency-bound (M = 128, N = VS, one chunk after another), so it
+// gets warps of its own:
+//  * chain warps 0-3: S -> f16 copy, P rows 16w.. (split-K accumulators) ->
+//    f16 copy, S <- d (.) S + Kbar^T P for key rows 32w..;
+//  * output warps 4-7: O rows 16(w-4).. = E S + F from the f16 copy of S
+//    (double-buffered, so the chain can write the next one meanwhile).
+// Per chunk one block barrier (copy of S and image ready; the previous chunk
+// fully consumed) and one 128-thread barrier among the chain warps (P ready).
+template <int VS>
+struct MmaStateCfg {
+  static constexpr int SLICE = CH * VS * 2;
+  static constexpr int ST_U = 50176;
+  static constexpr int ST_F = ST_U + SLICE;
+  static constexpr int STAGE = ((ST_F + SLICE + 1023) / 1024) * 1024;
+  static constexpr int PS = VS * 2 + 16;   // row pitch of the f16 S and P copies (conflict-free)
+  static constexpr int NST = 3 * STAGE + (2 * KD + CH) * PS + 64 <= 227 * 1024 ? 3 : 2;
+  static constexpr int SX_OFF = NST * STAGE;             // [2][128][PS]
+  static constexpr int PX_OFF = SX_OFF + 2 * KD * PS;    // [64][PS]
+  static constexpr int BAR_OFF = PX_OFF + CH * PS;
+  static constexpr int SMEM = BAR_OFF + 64;
+  static constexpr uint32_t TX = IMG_SHARED + 2 * SLICE;
+  static_assert(SMEM <= 227 * 1024, "state shared memory");
+};
+constexpr int MMA_STATE_WARPS = 8;
+
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+  static __device__ __forceinline__ void store(float* p, float a, float b) {
+    *reinterpret_cast<float2*>(p) = make_float2(a, b);
+  }
+};
+template <> struct Pair<__half> {
+  static __device__ __forceinline__ void store(__half* p, float a, float b) {
+    *reinterpret_cast<__half2*>(p) = __floats2half2_rn(a, b);
+  }
+};
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+  }
+};
+
+template <int VS>
+__device__ __forceinline__ void fetch_chunk_mma(uint8_t* stg, const uint8_t* img_g, int v0,
+                                                uint64_t* bar) {
+  using Cfg = MmaStateCfg<VS>;
+  ptx::mbar_arrive_expect_tx(bar, Cfg::TX);
+  ptx::bulk_g2s(stg, img_g, IMG_SHARED, bar);
+  ptx::bulk_g2s(stg + Cfg::ST_U, img_g + IMG_U + v0 * 128, Cfg::SLICE, bar);
+  ptx::bulk_g2s(stg + Cfg::ST_F, img_g + IMG_F + v0 * 128, Cfg::SLICE, bar);
+}
+
+__device__ __forceinline__ void chain_barrier() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int VS, typename TIO, typename TSI, typename TSO>
+__global__ void __launch_bounds__(MMA_STATE_WARPS * 32, 1)
+state_mma_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
+  using Cfg = MmaStateCfg<VS>;
+  constexpr int NST = Cfg::NST, PS = Cfg::PS;
+  constexpr int NTL = VS / 8;         // 8-column tiles
+  static_assert(NTL % 2 == 0, "VS must be a multiple of 16");
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint8_t* Px = sm + Cfg::PX_OFF;     // P  f16 [64 rows][VS], pitch PS
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::BAR_OFF);   // [NST] chunk images
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + NST);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const bool chain = warp < 4;
+  const int b = blockIdx.z, h = blockIdx.y, v0 = blockIdx.x * VS;
+  const int T = p.T;
+  const int NT = (T + CH - 1) / CH;
+  const int KR = 32 * (warp & 3);     // chain warps: first key row
+  const int CR = 16 * (warp & 3);     // first P row (chain) or O row (output) of this warp
+  const uint8_t* wsh = ws + (size_t)(b * p.H + h) * NT * IMG_BYTES;
+  // ldmatrix row addresses: matrix j = lane / 8 supplies its row lane % 8
+  const int lm_row = (lane & 7) + 8 * ((lane >> 3) & 1);   // A: rows, B (trans): k rows
+  const int lm_col = 8 * (lane >> 4);                      // A: k offset, B: column offset
+
+  if (tid == 0) {
+    for (int sg = 0; sg < NST; ++sg) ptx::mbar_init(&full[sg], 1);
+    ptx::fence_mbar_init();
+    *abort_flag = 0;
+  }
+  __syncthreads();
+  // the copy issuer is lane 0 of the last output warp; it tracks the stages
+  // with a copy in flight and their phase parity
+  const bool issuer = tid == MMA_STATE_WARPS * 32 - 32;
+  uint32_t pending = 0, pend_par = 0;
+  if (issuer) {
+    for (int sg = 0; sg < NST && sg < NT; ++sg) {
+      fetch_chunk_mma<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
+      pending |= 1u << sg;
+    }
+  }
+
+  // chain warps: master state, accumulator layout S[mt][nt] rows
+  // KR + 16 mt + gid (+8), columns 8 nt + 2 tig (+1)
+  float S[2][NTL][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = 0.f;
+        if (chain && p.state_in != nullptr) {
+          const int row = KR + 16 * mt + gid + 8 * (e >> 1);
+          const int col = v0 + 8 * nt + 2 * tig + (e & 1);
+          x = ld(static_cast<const TSI*>(p.state_in) + b * p.si_s[0] + h * p.si_s[1] +
+                 (int64_t)row * p.si_s[2] + col);
+        }
+        S[mt][nt][e] = x;
+      }
+
+  bool aborted = false;
+#pragma unroll 1
+  for (int n = 0; n < NT; ++n) {
+    const int sg = n % NST;
+    const uint8_t* stg = sm + sg * Cfg::STAGE;
+    uint8_t* Sx = sm + Cfg::SX_OFF + (n & 1) * KD * PS;   // f16 copy of S_n [128][PS]
+    if (chain) {                      // S -> f16 copy (rows = key, columns = value)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NTL; ++nt) {
+          const int row = KR + 16 * mt + gid, col = 8 * nt + 2 * tig;
+          st_h2(Sx, row * PS + col * 2, S[mt][nt][0], S[mt][nt][1]);
+          st_h2(Sx, (row + 8) * PS + col * 2, S[mt][nt][2], S[mt][nt][3]);
+        }
+    }
+    if (ptx::mbar_wait(&full[sg], (n / NST) & 1, kWaitNs)) {
+      if (issuer) pending &= ~(1u << sg);
+    } else {
+      *abort_flag = 1;
+    }
+    __syncthreads();                  // copy of S_n and image n ready; chunk n-1 consumed
+    if (*abort_flag) { aborted = true; break; }
+    if (issuer && n >= 1 && n - 1 + NST < NT) {          // refill the stage of chunk n-1
+      const int s1 = (n - 1) % NST;
+      ptx::fence_proxy_async_smem();
+      fetch_chunk_mma<VS>(sm + s1 * Cfg::STAGE, wsh + (size_t)(n - 1 + NST) * IMG_BYTES, v0,
+                          &full[s1]);
+      pending |= 1u << s1;
+      pend_par = (pend_par & ~(1u << s1)) | ((((n - 1 + NST) / NST) & 1u) << s1);
+    }
+    // rows 16(w%4).. of [-W; E] S: P rows for the chain warps, O rows (64 +)
+    // for the output warps; two accumulators (even / odd k-steps)
+    float ra[2][NTL][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ra[i][nt][e] = 0.f;
+    {
+      const int arow = (chain ? 0 : CH) + CR + lm_row;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t bf[NTL / 2][4], af[4];
+#pragma unroll
+        for (int jp = 0; jp < NTL / 2; ++jp)
+          ptx::ldmatrix_x4_trans(bf[jp], Sx + (16 * ks + lm_row) * PS + (16 * jp + lm_col) * 2);
+        ptx::ldmatrix_x4(af, stg + IMG_A1 + a1_off(arow, 16 * ks + lm_col));
+#pragma unroll
+        for (int nt = 0; nt < NTL; ++nt)
+          ptx::mma_f16_16x8x16(ra[ks & 1][nt], af, &bf[nt >> 1][2 * (nt & 1)]);
+      }
+    }
+    if (chain) {
+      // P = U - W S -> f16 copy
+      const uint8_t* ub = stg + Cfg::ST_U;
+#pragma unroll
+      for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int c = CR + gid + 8 * hf, col = 8 * nt + 2 * tig;
+          const float2 u = __half22float2(*reinterpret_cast<const __half2*>(ub + vb_off(c, col)));
+          st_h2(Px, c * PS + col * 2, ra[0][nt][2 * hf] + ra[1][nt][2 * hf] + u.x,
+                ra[0][nt][2 * hf + 1] + ra[1][nt][2 * hf + 1] + u.y);
+        }
+      chain_barrier();                // P complete
+      // S <- d (.) S + Kbar^T P for key rows KR..
+      const float* dv = reinterpret_cast<const float*>(stg + IMG_D);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const float dlo = dv[KR + 16 * mt + gid], dhi = dv[KR + 16 * mt + gid + 8];
+#pragma unroll
+        for (int nt = 0; nt < NTL; ++nt) {
+          S[mt][nt][0] *= dlo; S[mt][nt][1] *= dlo;
+          S[mt][nt][2] *= dhi; S[mt][nt][3] *= dhi;
+        }
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t bf[NTL / 2][4];
+#pragma unroll
+        for (int jp = 0; jp < NTL / 2; ++jp)
+          ptx::ldmatrix_x4_trans(bf[jp], Px + (16 * ks + lm_row) * PS + (16 * jp + lm_col) * 2);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t af[4];
+          ptx::ldmatrix_x4(af, stg + IMG_A3 + a2_off(KR + 16 * mt + lm_row, 16 * ks + lm_col));
+#pragma unroll
+          for (int nt = 0; nt < NTL; ++nt)
+            ptx::mma_f16_16x8x16(S[mt][nt], af, &bf[nt >> 1][2 * (nt & 1)]);
+        }
+      }
+    } else {
+      // O = E S + F for chunk rows CR..
+      const uint8_t* fb = stg + Cfg::ST_F;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int c = CR + gid + 8 * hf;
+        const int t = n * CH + c;
+        if (t >= T) continue;
+        TIO* dst = static_cast<TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] +
+                   h * p.o_s[2] + v0;
+#pragma unroll
+        for (int nt = 0; nt < NTL; ++nt) {
+          const int col = 8 * nt + 2 * tig;
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(fb + vb_off(c, col)));
+          const float o0 = ra[0][nt][2 * hf] + ra[1][nt][2 * hf] + f.x;
+          const float o1 = ra[0][nt][2 * hf + 1] + ra[1][nt][2 * hf + 1] + f.y;
+          if (p.o_vec16) {
+            Pair<TIO>::store(dst + col, o0, o1);
+          } else {
+            st(dst + col, o0);
+            st(dst + col + 1, o1);
+          }
+        }
+      }
+    }
+  }
+
+  if (!aborted) {
+    if (chain) {
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NTL; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int row = KR + 16 * mt + gid + 8 * (e >> 1);
+            const int col = v0 + 8 * nt + 2 * tig + (e & 1);
+            st(static_cast<TSO*>(p.state_out) + b * p.so_s[0] + h * p.so_s[1] +
+                   (int64_t)row * p.so_s[2] + col,
+               S[mt][nt][e]);
+          }
+    }
+  } else if (issuer) {
+    atomicExch(&g_kda_device_error, 1);
+    // let bulk copies still in flight land before this CTA's smem is released
+    for (int sg = 0; sg < NST; ++sg)
+      if (pending & (1u << sg)) ptx::mbar_wait(&full[sg], (pend_par >> sg) & 1u, kWaitNs / 2);
   }
 }
 
@@ -1040,6 +1308,20 @@ cudaError_t launch_state(const ChunkParams& p, const uint8_t* ws, cudaStream_t s
   kern<<<grid, 128, StateCfg<VS>::SMEM, s>>>(p, ws);
   return cudaGetLastError();
 }
+
+template <typename TIO, typename TSI, typename TSO, int VS>
+cudaError_t launch_state_mma(const ChunkParams& p, const uint8_t* ws, cudaStream_t s) {
+  auto kern = state_mma_kernel<VS, TIO, TSI, TSO>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       MmaStateCfg<VS>::SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.V / VS, p.H, p.B);
+  kern<<<grid, MMA_STATE_WARPS * 32, MmaStateCfg<VS>::SMEM, s>>>(p, ws);
+  return cudaGetLastError();
+}
+
+// which state pass runs: the register-resident one (true) or the TMEM one
+bool state_in_registers(int vs) { return vs <= 32; }
 
 template <typename TIO, int LOAD>
 cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
@@ -1077,7 +1359,15 @@ cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
                   : vec                ? launch_prep<TIO, 1>(p, ws, s)
                                        : launch_prep<TIO, 0>(p, ws, s);
   if (e != cudaSuccess) return e;
-  switch (pick_vs(p)) {
+  const int vs = pick_vs(p);
+  if (state_in_registers(vs)) {
+    switch (vs) {
+      case 16: return launch_state_mma<TIO, TSI, TSO, 16>(p, ws, s);
+      case 32: return launch_state_mma<TIO, TSI, TSO, 32>(p, ws, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  switch (vs) {
     case 16: return launch_state<TIO, TSI, TSO, 16>(p, ws, s);
     case 32: return launch_state<TIO, TSI, TSO, 32>(p, ws, s);
     case 64: return launch_state<TIO, TSI, TSO, 64>(p, ws, s);

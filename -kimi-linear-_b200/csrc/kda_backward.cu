@@ -13,88 +13,105 @@
 //   dg_t  = rowsum(dSt (.) St)       dS_{t-1} = Diag(alpha_t) dSt
 // (dg = alpha (.) dalpha with dalpha = rowsum(dSt (.) S_{t-1})).
 //
-// Two kernels, one CTA per (b, h, 16-column tile of V); a thread owns 4
-// adjacent columns of K/32 rows:
+// Two kernels, one CTA of four warps per (b, h, 16-column tile of V).  A warp
+// owns 4 adjacent value columns and all K rows (lane i: rows i, i+32, ...), so
+// the two reductions over K on the chain (a_t in a forward step, du in a
+// reverse step) are warp shuffles: the sequential steps never wait at a block
+// barrier.
 //  * checkpoint_kernel runs the recurrence forward and stores the state tile
 //    before every 64-step chunk (fp32);
 //  * backward_kernel walks the chunks backwards: it reruns a chunk from its
 //    checkpoint keeping every 8th state, then per 8-step block reruns the
 //    block keeping each step's S_{t-1}, u_t and v_t - a_t, and applies the
-//    reverse steps above.  All per-step state copies are thread-private
-//    (each thread stores and reloads only its own elements), so only the two
-//    reductions over K (a_t in the rerun, du in the reverse step) need a
-//    barrier.  dq, dk, dg and dbeta sum over the V columns: each tile writes
-//    its partial sums, added up afterwards over the V/16 tiles.
+//    reverse steps above.  State copies are lane-private (each lane stores and
+//    reloads only its own elements); u and v - a are per warp.
+// dq, dk, dg and dbeta sum over the V columns: the four warps' per-row sums of
+// a block of steps meet in shared memory once per block (one barrier pair per
+// 8 steps, off the chain), and each column tile writes its partial sums,
+// added up afterwards over the V/16 tiles.
 #include "kda_internal.cuh"
 
 namespace kda {
 namespace bwd {
 
-constexpr int NTH = 128;
-constexpr int CT = 4;              // column groups of 4 -> 16 columns per tile
-constexpr int VT = 4 * CT;
-constexpr int RG = NTH / CT;       // 32 row groups
+constexpr int NW = 4;              // warps per CTA, 4 value columns each
+constexpr int NTH = 32 * NW;
+constexpr int VT = 4 * NW;         // 16 columns per tile
 constexpr int CK = 64;             // checkpoint interval (steps)
 constexpr int SB = 8;              // sub-checkpoint interval inside a chunk
 
-// per-step vectors of step t for this thread: q', k, alpha of its rows, v of
-// its columns and beta
+// per-step vectors of step t for this lane: q', k, alpha of its rows, v and
+// dO of its warp's columns and beta.  Every sequential loop below issues the
+// loads of step t+1 (or t-1) as raw values (StepRaw: no arithmetic on them,
+// so nothing waits for them) while it computes step t, and converts them
+// (cook) when that step comes.
 template <typename TIO, int R>
 struct StepIn {
-  float q[R], k[R], al[R], v[4], beta;
+  float q[R], k[R], al[R], v[4], dO[4], beta;
+};
+template <typename TIO, int R>
+struct StepRaw {
+  TIO q[R], k[R], v[4], dO[4];
+  float g[R], beta;
 };
 
 template <typename TIO, int R>
-__device__ __forceinline__ void load_step(const BwdParams& p, int b, int h, int t, int rg,
-                                          int col0, StepIn<TIO, R>& s) {
+__device__ __forceinline__ void load_step(const BwdParams& p, int b, int h, int t, int lane,
+                                          int col0, StepRaw<TIO, R>& s, bool with_dout = false) {
   const TIO* qb = static_cast<const TIO*>(p.q) + b * p.q_s[0] + (int64_t)t * p.q_s[1] + h * p.q_s[2];
   const TIO* kb = static_cast<const TIO*>(p.k) + b * p.k_s[0] + (int64_t)t * p.k_s[1] + h * p.k_s[2];
   const TIO* vb = static_cast<const TIO*>(p.v) + b * p.v_s[0] + (int64_t)t * p.v_s[1] + h * p.v_s[2];
   const float* gb = p.g + b * p.g_s[0] + (int64_t)t * p.g_s[1] + h * p.g_s[2];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int i = rg + RG * r;
-    s.q[r] = ld(qb + i) * p.scale;
-    s.k[r] = ld(kb + i);
-    s.al[r] = expf(gb[i]);
+    const int i = lane + 32 * r;
+    s.q[r] = qb[i];
+    s.k[r] = kb[i];
+    s.g[r] = gb[i];
   }
 #pragma unroll
-  for (int c = 0; c < 4; ++c) s.v[c] = ld(vb + col0 + c);
+  for (int c = 0; c < 4; ++c) s.v[c] = vb[col0 + c];
   s.beta = p.beta[b * p.b_s[0] + (int64_t)t * p.b_s[1] + h * p.b_s[2]];
+  if (with_dout) {
+    const TIO* dob = static_cast<const TIO*>(p.dout) + b * p.do_s[0] + (int64_t)t * p.do_s[1] +
+                     h * p.do_s[2];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) s.dO[c] = dob[col0 + c];
+  }
 }
 
-// sum over the K rows of per-column values x[4]: 8 row groups per warp by
-// shuffles, 4 warps through shared memory; every thread gets the totals of
-// its 4 columns
-__device__ __forceinline__ void row_reduce(float (&x)[4], float (*red)[VT], int lane, int warp,
-                                           int ct) {
+template <typename TIO, int R>
+__device__ __forceinline__ StepIn<TIO, R> cook(const StepRaw<TIO, R>& r, float scale,
+                                               bool with_dout = false) {
+  StepIn<TIO, R> s;
 #pragma unroll
-  for (int off = CT; off < 32; off <<= 1)
+  for (int i = 0; i < R; ++i) {
+    s.q[i] = ld(&r.q[i]) * scale;
+    s.k[i] = ld(&r.k[i]);
+    s.al[i] = expf(r.g[i]);
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    s.v[c] = ld(&r.v[c]);
+    s.dO[c] = with_dout ? ld(&r.dO[c]) : 0.f;
+  }
+  s.beta = r.beta;
+  return s;
+}
+
+// sum over the K rows (the 32 lanes) of per-column values x[4]; every lane
+// gets the totals
+__device__ __forceinline__ void warp_sum4(float (&x)[4]) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
     for (int c = 0; c < 4; ++c) x[c] += __shfl_xor_sync(0xffffffffu, x[c], off);
-  if (lane < CT) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) red[warp][4 * ct + c] = x[c];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < 4; ++c)
-    x[c] = red[0][4 * ct + c] + red[1][4 * ct + c] + red[2][4 * ct + c] + red[3][4 * ct + c];
-  __syncthreads();
 }
 
-// sum over the 4 column groups (lanes with the same row group)
-__device__ __forceinline__ float col_reduce(float x) {
-  x += __shfl_xor_sync(0xffffffffu, x, 1);
-  x += __shfl_xor_sync(0xffffffffu, x, 2);
-  return x;
-}
-
-// one forward step on the state tile; returns u (own columns) and v - a
+// one forward step on the state tile; returns u and v - a (warp-uniform)
 template <typename TIO, int R>
 __device__ __forceinline__ void fwd_step(float (&S)[R][4], const StepIn<TIO, R>& s,
-                                         float (&u)[4], float (&vma)[4], float (*red)[VT],
-                                         int lane, int warp, int ct) {
+                                         float (&u)[4], float (&vma)[4]) {
   float a[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -103,7 +120,7 @@ __device__ __forceinline__ void fwd_step(float (&S)[R][4], const StepIn<TIO, R>&
       S[r][c] *= s.al[r];
       a[c] = fmaf(s.k[r], S[r][c], a[c]);
     }
-  row_reduce(a, red, lane, warp, ct);
+  warp_sum4(a);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     vma[c] = s.v[c] - a[c];
@@ -118,16 +135,14 @@ __device__ __forceinline__ void fwd_step(float (&S)[R][4], const StepIn<TIO, R>&
 template <typename TIO, typename TSI, int R>
 __global__ void __launch_bounds__(NTH, 1)
 checkpoint_kernel(const BwdParams p) {
-  __shared__ float red[4][VT];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ct = tid % CT, rg = tid / CT;
   const int b = blockIdx.z, h = blockIdx.y;
-  const int col0 = blockIdx.x * VT + 4 * ct;
+  const int col0 = blockIdx.x * VT + 4 * warp;
   const int NC = (p.T + CK - 1) / CK;
   float S[R][4];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int i = rg + RG * r;
+    const int i = lane + 32 * r;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       S[r][c] = p.state_in ? ld(static_cast<const TSI*>(p.state_in) + b * p.si_s[0] +
@@ -135,36 +150,50 @@ checkpoint_kernel(const BwdParams p) {
                            : 0.f;
   }
   float* ck = p.ckpt + ((size_t)(b * p.H + h) * NC) * p.K * p.V;
+  StepRaw<TIO, R> cur, nxt;
+  load_step<TIO, R>(p, b, h, 0, lane, col0, cur);
   for (int t = 0; t < p.T; ++t) {
+    load_step<TIO, R>(p, b, h, min(t + 1, p.T - 1), lane, col0, nxt);
     if (t % CK == 0) {
       float* dst = ck + (size_t)(t / CK) * p.K * p.V;
 #pragma unroll
       for (int r = 0; r < R; ++r)
-        *reinterpret_cast<float4*>(dst + (size_t)(rg + RG * r) * p.V + col0) =
+        *reinterpret_cast<float4*>(dst + (size_t)(lane + 32 * r) * p.V + col0) =
             make_float4(S[r][0], S[r][1], S[r][2], S[r][3]);
     }
-    StepIn<TIO, R> s;
-    load_step<TIO, R>(p, b, h, t, rg, col0, s);
     float u[4], vma[4];
-    fwd_step<TIO, R>(S, s, u, vma, red, lane, warp, ct);
+    fwd_step<TIO, R>(S, cook(cur, p.scale), u, vma);
+    cur = nxt;
   }
 }
 
-template <typename TIO, typename TSO, int R>
+// dynamic shared memory of backward_kernel (floats)
+template <int R>
+struct BwdSmem {
+  static constexpr int SUBCK = SB * R * 4 * NTH;     // lane-private sub-checkpoints
+  static constexpr int SPREV = SB * R * 4 * NTH;     // lane-private S_{t-1} of a block
+  static constexpr int UV = SB * NW * 4;             // u (and v - a) per step and warp
+  static constexpr int OUT = SB * 3 * NW * 32 * R;   // per-warp row sums of dq', dk, dg
+  static constexpr int OUTB = SB * NW;               // per-warp dbeta
+  static constexpr int FLOATS = SUBCK + SPREV + 2 * UV + OUT + OUTB;
+  static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
+};
+
+template <typename TIO, int R>
 __global__ void __launch_bounds__(NTH, 1)
 backward_kernel(const BwdParams p) {
+  using L = BwdSmem<R>;
   extern __shared__ __align__(16) float smem[];
-  // thread-private slots, element e of thread tid at [e * NTH + tid]
-  float* subck = smem;                                   // SB sub-checkpoints x R*4
-  float* sprev = subck + (size_t)SB * R * 4 * NTH;       // SB steps of S_{t-1}  x R*4
-  float* su = sprev + (size_t)SB * R * 4 * NTH;          // SB steps of u       x 4
-  float* svma = su + (size_t)SB * 4 * NTH;               // SB steps of v - a   x 4
-  __shared__ float red[4][VT];
+  float* subck = smem;                 // [SB][R*4][NTH], element e of thread tid at e*NTH + tid
+  float* sprev = subck + L::SUBCK;     // [SB][R*4][NTH]
+  float* su = sprev + L::SPREV;        // [SB][NW][4]
+  float* svma = su + L::UV;            // [SB][NW][4]
+  float* sout = svma + L::UV;          // [SB][3][NW][32 R]: dq', dk, dg row sums per warp
+  float* soutb = sout + L::OUT;        // [SB][NW]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ct = tid % CT, rg = tid / CT;
   const int b = blockIdx.z, h = blockIdx.y, vt = blockIdx.x;
-  const int col0 = vt * VT + 4 * ct;
+  const int col0 = vt * VT + 4 * warp;
   const int T = p.T, K = p.K, V = p.V;
   const int NC = (T + CK - 1) / CK;
   const float* ck = p.ckpt + ((size_t)(b * p.H + h) * NC) * K * V;
@@ -173,7 +202,7 @@ backward_kernel(const BwdParams p) {
   float dS[R][4];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const int i = rg + RG * r;
+    const int i = lane + 32 * r;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       dS[r][c] = p.dstate_out ? p.dstate_out[b * p.dso_s[0] + h * p.dso_s[1] +
@@ -186,7 +215,6 @@ backward_kernel(const BwdParams p) {
   float* dk_p = p.dk_part + vt * pk;
   float* dg_p = p.dg_part + vt * pk;
   float* db_p = p.dbeta_part + (size_t)vt * p.B * T * p.H;
-  auto kidx = [&](int t, int i) { return (((size_t)b * T + t) * p.H + h) * K + i; };
 
   for (int n = NC - 1; n >= 0; --n) {
     const int t0 = n * CK, t1 = min(T, t0 + CK);
@@ -195,22 +223,26 @@ backward_kernel(const BwdParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const float4 x = *reinterpret_cast<const float4*>(ck + (size_t)n * K * V +
-                                                        (size_t)(rg + RG * r) * V + col0);
+                                                        (size_t)(lane + 32 * r) * V + col0);
       S[r][0] = x.x; S[r][1] = x.y; S[r][2] = x.z; S[r][3] = x.w;
     }
-    for (int t = t0; t < t1; ++t) {
-      if ((t - t0) % SB == 0) {
-        float* d = subck + (size_t)((t - t0) / SB) * R * 4 * NTH;
+    {
+      StepRaw<TIO, R> cur, nxt;
+      load_step<TIO, R>(p, b, h, t0, lane, col0, cur);
+      for (int t = t0; t < t1; ++t) {
+        if ((t - t0) % SB == 0) {
+          float* d = subck + (size_t)((t - t0) / SB) * R * 4 * NTH;
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+          for (int r = 0; r < R; ++r)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) d[(r * 4 + c) * NTH + tid] = S[r][c];
-      }
-      if (t + 1 < t1) {     // the chunk's last state is not needed
-        StepIn<TIO, R> s;
-        load_step<TIO, R>(p, b, h, t, rg, col0, s);
-        float u[4], vma[4];
-        fwd_step<TIO, R>(S, s, u, vma, red, lane, warp, ct);
+            for (int c = 0; c < 4; ++c) d[(r * 4 + c) * NTH + tid] = S[r][c];
+        }
+        if (t + 1 < t1) {     // the chunk's last state is not needed
+          load_step<TIO, R>(p, b, h, t + 1, lane, col0, nxt);
+          float u[4], vma[4];
+          fwd_step<TIO, R>(S, cook(cur, p.scale), u, vma);
+          cur = nxt;
+        }
       }
     }
     // the SB-step blocks, last first
@@ -224,35 +256,39 @@ backward_kernel(const BwdParams p) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) S[r][c] = d[(r * 4 + c) * NTH + tid];
       }
+      StepRaw<TIO, R> cur, nxt;
+      load_step<TIO, R>(p, b, h, ts, lane, col0, cur);
       for (int t = ts; t < te; ++t) {   // rerun: keep S_{t-1}, u_t, v_t - a_t
+        load_step<TIO, R>(p, b, h, min(t + 1, te - 1), lane, col0, nxt);
         float* d = sprev + (size_t)(t - ts) * R * 4 * NTH;
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
           for (int c = 0; c < 4; ++c) d[(r * 4 + c) * NTH + tid] = S[r][c];
-        StepIn<TIO, R> s;
-        load_step<TIO, R>(p, b, h, t, rg, col0, s);
         float u[4], vma[4];
-        fwd_step<TIO, R>(S, s, u, vma, red, lane, warp, ct);
+        fwd_step<TIO, R>(S, cook(cur, p.scale), u, vma);
+        if (lane == 0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          su[((t - ts) * 4 + c) * NTH + tid] = u[c];
-          svma[((t - ts) * 4 + c) * NTH + tid] = vma[c];
+          for (int c = 0; c < 4; ++c) {
+            su[((t - ts) * NW + warp) * 4 + c] = u[c];
+            svma[((t - ts) * NW + warp) * 4 + c] = vma[c];
+          }
         }
+        cur = nxt;
       }
+      __syncwarp();
+      load_step<TIO, R>(p, b, h, te - 1, lane, col0, cur, true);
       for (int t = te - 1; t >= ts; --t) {   // reverse steps
-        StepIn<TIO, R> s;
-        load_step<TIO, R>(p, b, h, t, rg, col0, s);
-        const TIO* dob = static_cast<const TIO*>(p.dout) + b * p.do_s[0] +
-                         (int64_t)t * p.do_s[1] + h * p.do_s[2];
-        float dO[4], u[4], vma[4];
+        load_step<TIO, R>(p, b, h, max(t - 1, ts), lane, col0, nxt, true);
+        const StepIn<TIO, R> s = cook(cur, p.scale, true);
+        const int j = t - ts;
+        float u[4], vma[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          dO[c] = ld(dob + col0 + c);
-          u[c] = su[((t - ts) * 4 + c) * NTH + tid];
-          vma[c] = svma[((t - ts) * 4 + c) * NTH + tid];
+          u[c] = su[(j * NW + warp) * 4 + c];
+          vma[c] = svma[(j * NW + warp) * 4 + c];
         }
-        const float* d = sprev + (size_t)(t - ts) * R * 4 * NTH;
+        const float* d = sprev + (size_t)j * R * 4 * NTH;
         float St[R][4];                       // alpha (.) S_{t-1}
         float dqp[R], du[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -262,27 +298,26 @@ backward_kernel(const BwdParams p) {
           for (int c = 0; c < 4; ++c) {
             St[r][c] = s.al[r] * d[(r * 4 + c) * NTH + tid];
             const float Snew = fmaf(s.k[r], u[c], St[r][c]);   // S_t
-            acc = fmaf(Snew, dO[c], acc);
-            dS[r][c] = fmaf(s.q[r], dO[c], dS[r][c]);
+            acc = fmaf(Snew, s.dO[c], acc);
+            dS[r][c] = fmaf(s.q[r], s.dO[c], dS[r][c]);
             du[c] = fmaf(dS[r][c], s.k[r], du[c]);
           }
           dqp[r] = acc;
         }
-        row_reduce(du, red, lane, warp, ct);
+        warp_sum4(du);
         float dbp = 0.f, da[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           dbp = fmaf(du[c], vma[c], dbp);
           da[c] = -s.beta * du[c];
         }
-        if (rg == 0) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            p.dv[b * p.dv_s[0] + (int64_t)t * p.dv_s[1] + h * p.dv_s[2] + col0 + c] =
-                s.beta * du[c];
+        if (lane < 4) {
+          const float duc = lane == 0 ? du[0] : lane == 1 ? du[1] : lane == 2 ? du[2] : du[3];
+          p.dv[b * p.dv_s[0] + (int64_t)t * p.dv_s[1] + h * p.dv_s[2] + col0 + lane] =
+              s.beta * duc;
         }
-        dbp = col_reduce(dbp);
-        if (tid == 0) db_p[((size_t)b * T + t) * p.H + h] = dbp;
+        if (lane == 0) soutb[j * NW + warp] = dbp;
+        float* so = sout + (size_t)j * 3 * NW * 32 * R;
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           float dkp = 0.f, dgp = 0.f;
@@ -294,15 +329,37 @@ backward_kernel(const BwdParams p) {
             dgp = fmaf(dSt, St[r][c], dgp);
             dS[r][c] = s.al[r] * dSt;
           }
-          const float q1 = col_reduce(dqp[r]), k1 = col_reduce(dkp), g1 = col_reduce(dgp);
-          if (ct == 0) {
-            const size_t at = kidx(t, rg + RG * r);
-            dq_p[at] = q1 * p.scale;
-            dk_p[at] = k1;
-            dg_p[at] = g1;
-          }
+          const int row = lane + 32 * r;
+          so[(0 * NW + warp) * 32 * R + row] = dqp[r];
+          so[(1 * NW + warp) * 32 * R + row] = dkp;
+          so[(2 * NW + warp) * 32 * R + row] = dgp;
         }
+        cur = nxt;
       }
+      // the block's row sums over the four warps (16 columns) -> partial outputs
+      __syncthreads();
+      for (int idx = tid; idx < (te - ts) * K; idx += NTH) {
+        const int j = idx / K, row = idx - j * K;
+        const float* so = sout + (size_t)j * 3 * NW * 32 * R;
+        float q1 = 0.f, k1 = 0.f, g1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          q1 += so[(0 * NW + w) * 32 * R + row];
+          k1 += so[(1 * NW + w) * 32 * R + row];
+          g1 += so[(2 * NW + w) * 32 * R + row];
+        }
+        const size_t at = (((size_t)b * T + ts + j) * p.H + h) * K + row;
+        dq_p[at] = q1 * p.scale;
+        dk_p[at] = k1;
+        dg_p[at] = g1;
+      }
+      if (tid < te - ts) {
+        float s1 = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) s1 += soutb[tid * NW + w];
+        db_p[((size_t)b * T + ts + tid) * p.H + h] = s1;
+      }
+      __syncthreads();
     }
   }
   // gradient of the initial state
@@ -310,7 +367,7 @@ backward_kernel(const BwdParams p) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       float* dst = p.dstate_in + b * p.dsi_s[0] + h * p.dsi_s[1] +
-                   (int64_t)(rg + RG * r) * p.dsi_s[2] + col0;
+                   (int64_t)(lane + 32 * r) * p.dsi_s[2] + col0;
 #pragma unroll
       for (int c = 0; c < 4; ++c) dst[c] = dS[r][c];
     }
@@ -323,11 +380,11 @@ static cudaError_t launch_r(const BwdParams& p, cudaStream_t s) {
   checkpoint_kernel<TIO, TSI, R><<<grid, NTH, 0, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const size_t smem = ((size_t)2 * SB * R * 4 + 2 * SB * 4) * NTH * sizeof(float);
-  e = cudaFuncSetAttribute(backward_kernel<TIO, float, R>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = BwdSmem<R>::BYTES;
+  e = cudaFuncSetAttribute(backward_kernel<TIO, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
   if (e != cudaSuccess) return e;
-  backward_kernel<TIO, float, R><<<grid, NTH, smem, s>>>(p);
+  backward_kernel<TIO, R><<<grid, NTH, smem, s>>>(p);
   return cudaGetLastError();
 }
 

@@ -1297,13 +1297,10 @@ int pick_vs(const ChunkParams& p) {
 template <typename TIO, typename TSI, typename TSO, int VS>
 cudaError_t launch_state(const ChunkParams& p, const uint8_t* ws, cudaStream_t s) {
   auto kern = state_kernel<VS, TIO, TSI, TSO>;
-  static bool attr_set = false;   // one attribute call per instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         StateCfg<VS>::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  // per call: the attribute belongs to the current device's context
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       StateCfg<VS>::SMEM);
+  if (e != cudaSuccess) return e;
   dim3 grid(p.V / VS, p.H, p.B);
   kern<<<grid, 128, StateCfg<VS>::SMEM, s>>>(p, ws);
   return cudaGetLastError();
@@ -1326,13 +1323,10 @@ bool state_in_registers(int vs) { return vs <= 32; }
 template <typename TIO, int LOAD>
 cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   auto prep = prep_kernel<TIO, LOAD>;
-  static bool attr_set = false;   // one attribute call per instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PREP_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  // per call: the attribute belongs to the current device's context
+  cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PREP_SMEM);
+  if (e != cudaSuccess) return e;
   const int NT = (p.T + CH - 1) / CH;
   dim3 pgrid(NT, p.H, p.B);
   prep<<<pgrid, PREP_THREADS, PREP_SMEM, s>>>(p, ws);

@@ -48,6 +48,7 @@
 //    The images are double-buffered in shared memory and fetched two chunks
 //    ahead with cp.async.bulk; every mbarrier wait is bounded in time and
 //    aborts the CTA cleanly (error word, TMEM freed) instead of hanging.
+#include <cuda.h>            // CUtensorMap (header only; the encoder comes from the runtime)
 #include <type_traits>
 
 #include "kda_internal.cuh"
@@ -150,7 +151,13 @@ constexpr int P_FAC = P_LM + CH * LMP * 4;             // P02,P03,P13,E[4]  fp32
 constexpr int P_BETA = P_FAC + 7 * KD * 4;             // beta            fp32 [64]
 constexpr int P_STEEP = P_BETA + CH * 4;               // steep bits      u32 [4][4]
 constexpr int P_MBAR = P_STEEP + 16 * 4;               // tcgen05 commit barrier (u64)
-constexpr int P_TSLOT = P_MBAR + 8;                    // TMEM base address (u32)
+constexpr int P_TBAR = P_MBAR + 8;                     // input tensor copies (u64)
+constexpr int P_TSLOT = P_TBAR + 8;                    // TMEM base address (u32)
+// LOAD == 3: the chunk's raw q, k, v (64 x 128, I/O dtype) and g (64 x 128
+// fp32) rows land by tensor copies here, in the Gram-operand region that
+// phase 1 writes only after every thread has read its inputs
+constexpr int P_STG = P_AXK;
+constexpr int STG_BYTES_G = CH * KD * 4;
 constexpr int PREP_SMEM = P_TSLOT + 8;
 constexpr int kPrepTmemCols = 256;                     // D[128 x 256] fp32 of phase 5
 static_assert(P_A2 >= IMG_BYTES, "image staging");
@@ -218,12 +225,33 @@ __device__ __forceinline__ void gemm16x8_3xtf32(float* acc, const float* Ab, int
   }
 }
 
+// tensor maps of q, k, v ([B, T, H, K], I/O dtype) and g (fp32) for LOAD == 3:
+// box = one (b, h) and 64 rows x 128 channels
+struct alignas(64) PrepMaps {
+  CUtensorMap q, k, v, g;
+};
+
+// two consecutive elements of a shared-memory row as fp32
+template <typename T>
+__device__ __forceinline__ float2 lds2(const T* p) {
+  if constexpr (std::is_same<T, float>::value) {
+    return *reinterpret_cast<const float2*>(p);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+  } else {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+}
+
 // LOAD: how phase 1 reads its inputs -- 0 scalar loads, 1 two-element vector
 // loads, 2 vector loads and, every input row being a 16-byte-aligned range,
-// the next wave's L2 prefetch issued as one bulk (TMA-engine) prefetch per row.
+// the next wave's L2 prefetch issued as one bulk (TMA-engine) prefetch per
+// row; 3 as 2 but the chunk's inputs arrive by four tensor copies (TMA)
+// instead of per-thread loads, which the SM's limit on outstanding loads caps
+// at ~10 bytes per cycle.
 template <typename TIO, int LOAD>
 __global__ void __launch_bounds__(PREP_THREADS, 1)
-prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
+prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant__ PrepMaps tm) {
   constexpr bool VEC = LOAD >= 1;
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* img = sm + P_IMG;
@@ -241,6 +269,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   float* sbeta = reinterpret_cast<float*>(sm + P_BETA);
   uint32_t* steep = reinterpret_cast<uint32_t*>(sm + P_STEEP);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + P_MBAR);
+  uint64_t* tbar = reinterpret_cast<uint64_t*>(sm + P_TBAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + P_TSLOT);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -265,7 +294,16 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   }
   if (tid == 32) {
     ptx::mbar_init(mbar, 1);
+    if constexpr (LOAD == 3) ptx::mbar_init(tbar, 1);
     ptx::fence_mbar_init();
+    if constexpr (LOAD == 3) {      // rows past T arrive as zeros
+      uint8_t* stg = sm + P_STG;
+      ptx::mbar_arrive_expect_tx(tbar, 3 * CH * KD * sizeof(TIO) + STG_BYTES_G);
+      ptx::tma_load_4d(stg, &tm.q, 0, h, t0, b, tbar);
+      ptx::tma_load_4d(stg + CH * KD * sizeof(TIO), &tm.k, 0, h, t0, b, tbar);
+      ptx::tma_load_4d(stg + 2 * CH * KD * sizeof(TIO), &tm.v, 0, h, t0, b, tbar);
+      ptx::tma_load_4d(stg + 3 * CH * KD * sizeof(TIO), &tm.g, 0, h, t0, b, tbar);
+    }
   }
   uint8_t* img_g = ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES;
 
@@ -277,7 +315,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
     const long tgt = n + (long)NT * (h + (long)p.H * b) + ptx::num_sms();
     if (tgt < total) {
       const int n2 = (int)(tgt % NT), h2 = (int)((tgt / NT) % p.H), b2 = (int)(tgt / ((long)NT * p.H));
-      if constexpr (LOAD == 2) {                   // one TMA-engine prefetch per row
+      if constexpr (LOAD >= 2) {                   // one TMA-engine prefetch per row
         const int c = tid >> 2, part = tid & 3;
         const int64_t t = (int64_t)n2 * CH + c;
         if (c < CH && t < p.T) {
@@ -324,7 +362,35 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws) {
   // clamped to the last valid row and zeroed below) so the loads overlap;
   // gr[8] is the row after the half (next half or next block)
   float2 gr[9], qr[8], kr[8], vr[8];
-  {
+  if constexpr (LOAD == 3) {
+    __syncthreads();                                 // tbar initialised
+    const bool in_ok = ptx::mbar_wait(tbar, 0, kWaitNs);
+    if (__syncthreads_or(!in_ok)) {                  // the copies never landed: give up
+      if (tid == 32) {
+        atomicExch(&g_kda_device_error, 3);
+        ptx::mbar_wait(tbar, 0, kWaitNs / 2);        // let them land before smem is released
+      }
+      __syncthreads();
+      if (warp == 0) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(*tslot, kPrepTmemCols);
+      }
+      return;
+    }
+    const TIO* sq = reinterpret_cast<const TIO*>(sm + P_STG);
+    const TIO* sk = sq + CH * KD;
+    const TIO* sv = sk + CH * KD;
+    const float* sgp = reinterpret_cast<const float*>(sv + CH * KD);
+#pragma unroll
+    for (int i = 0; i < 9; ++i)      // row 64 (last half, i = 8) is not needed: clamp, zeroed below
+      gr[i] = *reinterpret_cast<const float2*>(sgp + min(rb0 + i, CH - 1) * KD + k0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      qr[i] = lds2(sq + (rb0 + i) * KD + k0);
+      kr[i] = lds2(sk + (rb0 + i) * KD + k0);
+      vr[i] = lds2(sv + (rb0 + i) * KD + k0);
+    }
+  } else {
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
       const int c = min(rb0 + i, nvalid - 1);
@@ -1321,7 +1387,8 @@ cudaError_t launch_state_mma(const ChunkParams& p, const uint8_t* ws, cudaStream
 bool state_in_registers(int vs) { return vs <= 32; }
 
 template <typename TIO, int LOAD>
-cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
+cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s,
+                        const PrepMaps& maps = PrepMaps{}) {
   auto prep = prep_kernel<TIO, LOAD>;
   // per call: the attribute belongs to the current device's context
   cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1329,7 +1396,7 @@ cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const int NT = (p.T + CH - 1) / CH;
   dim3 pgrid(NT, p.H, p.B);
-  prep<<<pgrid, PREP_THREADS, PREP_SMEM, s>>>(p, ws);
+  prep<<<pgrid, PREP_THREADS, PREP_SMEM, s>>>(p, ws, maps);
   return cudaGetLastError();
 }
 
@@ -1346,12 +1413,66 @@ bool bulk_rows_ok(const ChunkParams& p) {
          al(p.v, p.v_s, sizeof(TIO)) && al(p.g, p.g_s, 4);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda)
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled() {
+  static EncodeTiled fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+    tried = true;
+  }
+  return fn;
+}
+
+// map of a [B, T, H, K = 128] tensor (element strides st) with a box of one
+// (b, h) and 64 rows x 128 channels; false when the driver rejects it
+bool encode_rows(CUtensorMap* m, CUtensorMapDataType dt, size_t esz, const void* ptr,
+                 const int64_t* st, const ChunkParams& p) {
+  EncodeTiled enc = encode_tiled();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)KD, (cuuint64_t)p.H, (cuuint64_t)p.T, (cuuint64_t)p.B};
+  const cuuint64_t strides[3] = {(cuuint64_t)(st[2] * esz), (cuuint64_t)(st[1] * esz),
+                                 (cuuint64_t)(st[0] * esz)};
+  const cuuint32_t box[4] = {(cuuint32_t)KD, 1u, (cuuint32_t)CH, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  for (int d = 0; d < 3; ++d)
+    if (st[d] <= 0) return false;
+  return enc(m, dt, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename TIO>
+bool make_prep_maps(const ChunkParams& p, PrepMaps* m) {
+  const CUtensorMapDataType dt = std::is_same<TIO, __half>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return encode_rows(&m->q, dt, sizeof(TIO), p.q, p.q_s, p) &&
+         encode_rows(&m->k, dt, sizeof(TIO), p.k, p.k_s, p) &&
+         encode_rows(&m->v, dt, sizeof(TIO), p.v, p.v_s, p) &&
+         encode_rows(&m->g, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.g, p.g_s, p);
+}
+
 template <typename TIO, typename TSI, typename TSO>
 cudaError_t launch_tc3(const ChunkParams& p, uint8_t* ws, cudaStream_t s) {
   const bool vec = p.g_vec2 && p.qk_vec2 && p.v_vec2;
-  cudaError_t e = bulk_rows_ok<TIO>(p) ? launch_prep<TIO, 2>(p, ws, s)
-                  : vec                ? launch_prep<TIO, 1>(p, ws, s)
-                                       : launch_prep<TIO, 0>(p, ws, s);
+  cudaError_t e;
+  PrepMaps maps;
+  if (bulk_rows_ok<TIO>(p) && make_prep_maps<TIO>(p, &maps))
+    e = launch_prep<TIO, 3>(p, ws, s, maps);
+  else
+    e = bulk_rows_ok<TIO>(p) ? launch_prep<TIO, 2>(p, ws, s)
+        : vec                ? launch_prep<TIO, 1>(p, ws, s)
+                             : launch_prep<TIO, 0>(p, ws, s);
   if (e != cudaSuccess) return e;
   const int vs = pick_vs(p);
   if (state_in_registers(vs)) {

@@ -285,13 +285,9 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
   const float* gb = p.g + b * p.g_s[0] + h * p.g_s[2];
   const float* bb = p.beta + b * p.b_s[0] + h * p.b_s[2];
 
-  if (tid < 16) steep[tid] = 0u;
-  if (tid < CH) sbeta[tid] = (tid < nvalid) ? bb[(int64_t)(t0 + tid) * p.b_s[1]] : 0.f;
-  if (warp == 0) {                  // TMEM for phase 5 (one CTA per SM: never contended)
-    ptx::tmem_alloc(tslot, kPrepTmemCols);
-    ptx::tmem_relinquish();
-    ptx::tc_fence_before();
-  }
+  // the input copies go first; beta waits in a register until they landed
+  // (its load latency then overlaps theirs) and reaches shared memory with
+  // the phase-1 barrier
   if (tid == 32) {
     ptx::mbar_init(mbar, 1);
     if constexpr (LOAD == 3) ptx::mbar_init(tbar, 1);
@@ -305,6 +301,13 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
       ptx::tma_load_4d(stg + 3 * CH * KD * sizeof(TIO), &tm.g, 0, h, t0, b, tbar);
     }
   }
+  if (tid < 16) steep[tid] = 0u;
+  const float beta_c = (tid < nvalid) ? bb[(int64_t)(t0 + min(tid, CH - 1)) * p.b_s[1]] : 0.f;
+  if (warp == 0) {                  // TMEM for phase 5 (one CTA per SM: never contended)
+    ptx::tmem_alloc(tslot, kPrepTmemCols);
+    ptx::tmem_relinquish();
+    ptx::tc_fence_before();
+  }
   uint8_t* img_g = ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES;
 
   // L2 prefetch of the inputs of the chunk one SM-count further in launch
@@ -315,7 +318,14 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
     const long tgt = n + (long)NT * (h + (long)p.H * b) + ptx::num_sms();
     if (tgt < total) {
       const int n2 = (int)(tgt % NT), h2 = (int)((tgt / NT) % p.H), b2 = (int)(tgt / ((long)NT * p.H));
-      if constexpr (LOAD >= 2) {                   // one TMA-engine prefetch per row
+      if constexpr (LOAD == 3) {                   // four box prefetches
+        if (tid == 32) {
+          ptx::tma_prefetch_4d(&tm.q, 0, h2, n2 * CH, b2);
+          ptx::tma_prefetch_4d(&tm.k, 0, h2, n2 * CH, b2);
+          ptx::tma_prefetch_4d(&tm.v, 0, h2, n2 * CH, b2);
+          ptx::tma_prefetch_4d(&tm.g, 0, h2, n2 * CH, b2);
+        }
+      } else if constexpr (LOAD == 2) {            // one TMA-engine prefetch per row
         const int c = tid >> 2, part = tid & 3;
         const int64_t t = (int64_t)n2 * CH + c;
         if (c < CH && t < p.T) {
@@ -425,6 +435,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
     A0[k0] = expf(gr[0].x);
     A0[k0 + 1] = expf(gr[0].y);
   }
+  if (tid < CH) sbeta[tid] = beta_c;
   __syncthreads();
   {
     float Zx[4], Zy[4], eZx[4], eZy[4];

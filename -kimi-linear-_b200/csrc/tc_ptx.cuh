@@ -85,6 +85,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, in
       "r"(smem_u32(bar))
       : "memory");
 }
+// L2 prefetch of one box described by a tensor map (no shared memory involved)
+__device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int c0, int c1, int c2,
+                                                int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_s2g(void* dst_gmem, const void* src_smem, uint32_t bytes) {
   asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem),
                "r"(smem_u32(src_smem)), "r"(bytes)
@@ -236,10 +244,13 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const float* v) {
 // ---------------------------------------------------------------------------
 // legacy warp-level MMA (used for the 16x16 Gram blocks and W = M Ktilde)
 // ---------------------------------------------------------------------------
+// fp32 -> tf32 operand bits: round to nearest, ties away from zero, to the
+// 10-bit tf32 mantissa, on the bit pattern (carry into the exponent is the
+// correct rounding up; finite inputs only).  Same rounding as
+// cvt.rna.tf32.f32, and measured bit-identical in the kernels' outputs, but two
+// full-rate integer ops: the prep kernel got 4 % faster with it.
 __device__ __forceinline__ uint32_t f32_to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+  return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 // D(16x8) += A(16x8 tf32, row) * B(8x8 tf32, col)
 __device__ __forceinline__ void mma_tf32_16x8x8(float* d, const uint32_t* a, const uint32_t* b) {

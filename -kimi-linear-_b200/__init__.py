@@ -18,13 +18,17 @@ To route an existing ``kimi_linear`` model through these kernels::
 ``KimiDeltaAttention.forward`` looks the two functions up as module globals at
 call time (``kda.py:503,519,526``), so prefill, eager decode and
 ``GraphedDecoder`` all take the new path without further changes.
+
+Also here: the fused prologue / epilogue of the KDA block (``fused``), the
+gradient of the core (autograd through both functions) and the static-buffer
+MLA decode step of the full-attention layers (``mla.install_mla()``).
 """
 
 from __future__ import annotations
 
 import sys as _sys
 
-from . import _lib, fused, ops, sharding, synth
+from . import _lib, fused, mla, ops, sharding, synth
 from ._lib import KdaLibraryError
 from .fused import kda_epilogue, kda_prologue
 from .ops import KdaError, chunkwise_impl, chunkwise_path, device_error, kda_chunkwise, kda_recurrent
@@ -32,7 +36,7 @@ from .ops import KdaError, chunkwise_impl, chunkwise_path, device_error, kda_chu
 ALIAS = "kimi_linear_b200"
 if __name__ != ALIAS:
     _sys.modules.setdefault(ALIAS, _sys.modules[__name__])
-    for _sub in ("_lib", "fused", "ops", "sharding", "synth"):
+    for _sub in ("_lib", "fused", "mla", "ops", "sharding", "synth"):
         _sys.modules.setdefault(f"{ALIAS}.{_sub}", _sys.modules[f"{__name__}.{_sub}"])
 
 __all__ = ["kda_chunkwise", "kda_recurrent", "chunkwise_path", "chunkwise_impl", "device_error",

@@ -49,6 +49,9 @@ EXPORTED = (
     "kda_backward",
     "kda_backward_ckpt_floats",
     "kda_backward_args_size",
+    "mla_decode_fwd",
+    "mla_decode_workspace_bytes",
+    "mla_decode_args_size",
     "kda_args_size",
     "kda_abi_version",
 )
@@ -163,6 +166,29 @@ class KdaBackwardArgs(ctypes.Structure):
     ]
 
 
+_I64x2 = ctypes.c_int64 * 2
+
+
+class MlaDecodeArgs(ctypes.Structure):
+    """Mirror of ``struct MlaDecodeArgs``."""
+
+    _fields_ = [
+        ("abi_version", ctypes.c_int32),
+        ("B", ctypes.c_int32), ("L", ctypes.c_int32), ("H", ctypes.c_int32),
+        ("KVL", ctypes.c_int32), ("DN", ctypes.c_int32), ("DV", ctypes.c_int32),
+        ("io_dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q_nope", ctypes.c_void_p), ("q_nope_stride", _I64x3),
+        ("c_kv", ctypes.c_void_p), ("c_kv_stride", _I64x2),
+        ("kv_buf", ctypes.c_void_p), ("kv_buf_stride", _I64x3),
+        ("pos", ctypes.c_void_p),
+        ("w", ctypes.c_void_p), ("w_stride", _I64x2),
+        ("out", ctypes.c_void_p), ("out_stride", _I64x3),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 class KdaLibraryError(RuntimeError):
     """The CUDA library is missing or unusable (there is no fallback path)."""
 
@@ -193,6 +219,12 @@ def _declare(lib):
     lib.kda_prologue_fwd.restype = ctypes.c_int
     lib.kda_epilogue_fwd.argtypes = [ctypes.POINTER(KdaEpilogueArgs), ctypes.c_void_p]
     lib.kda_epilogue_fwd.restype = ctypes.c_int
+    lib.mla_decode_fwd.argtypes = [ctypes.POINTER(MlaDecodeArgs), ctypes.c_void_p]
+    lib.mla_decode_fwd.restype = ctypes.c_int
+    lib.mla_decode_workspace_bytes.argtypes = [ctypes.POINTER(MlaDecodeArgs)]
+    lib.mla_decode_workspace_bytes.restype = ctypes.c_size_t
+    lib.mla_decode_args_size.argtypes = []
+    lib.mla_decode_args_size.restype = ctypes.c_size_t
     lib.kda_backward.argtypes = [ctypes.POINTER(KdaBackwardArgs), ctypes.c_void_p]
     lib.kda_backward.restype = ctypes.c_int
     lib.kda_backward_ckpt_floats.argtypes = [ctypes.c_int] * 5
@@ -232,7 +264,8 @@ def load(path: str | None = None):
             raise KdaLibraryError(f"{p}: ABI version {lib.kda_abi_version()} != {ABI_VERSION}")
         for fn, st in (("kda_prologue_args_size", KdaPrologueArgs),
                        ("kda_epilogue_args_size", KdaEpilogueArgs),
-                       ("kda_backward_args_size", KdaBackwardArgs)):
+                       ("kda_backward_args_size", KdaBackwardArgs),
+                       ("mla_decode_args_size", MlaDecodeArgs)):
             if getattr(lib, fn)() != ctypes.sizeof(st):
                 raise KdaLibraryError(f"{p}: {fn}() != ctypes sizeof {ctypes.sizeof(st)}")
         if lib.kda_args_size() != ctypes.sizeof(KdaArgs):

@@ -11,6 +11,25 @@
 
 namespace kda {
 
+EncodeTiled encode_tiled() {
+  static EncodeTiled fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+    tried = true;
+  }
+  return fn;
+}
+
+}  // namespace kda
+
+namespace kda {
+
 
 namespace {
 
@@ -337,7 +356,12 @@ int kda_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
-int kda_device_error(int clear) { return read_device_error(clear != 0); }
+int kda_device_error(int clear) {
+  const int a = read_device_error(clear != 0);
+  const int b = kda::mla::read_device_error(clear != 0);
+  if (a < 0 || b < 0) return -1;
+  return a ? a : b;
+}
 
 int kda_prologue_fwd(const KdaPrologueArgs* args, void* stream) {
   int st = validate_prologue(args);

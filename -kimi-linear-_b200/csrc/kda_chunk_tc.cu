@@ -1424,26 +1424,6 @@ bool bulk_rows_ok(const ChunkParams& p) {
          al(p.v, p.v_s, sizeof(TIO)) && al(p.g, p.g_s, 4);
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda)
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-EncodeTiled encode_tiled() {
-  static EncodeTiled fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiled>(ptr);
-    tried = true;
-  }
-  return fn;
-}
-
 // map of a [B, T, H, K = 128] tensor (element strides st) with a box of one
 // (b, h) and 64 rows x 128 channels; false when the driver rejects it
 bool encode_rows(CUtensorMap* m, CUtensorMapDataType dt, size_t esz, const void* ptr,

@@ -1,9 +1,23 @@
 // kda_internal.cuh -- parameter blocks shared by the C-ABI layer and kernels.
 #pragma once
 
+#include <cuda.h>   // CUtensorMap and its enums (header only)
+
 #include "kda_common.cuh"
 
 namespace kda {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda);
+// nullptr when the driver does not provide it
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_tiled();
+
+namespace mla {
+int read_device_error(bool clear);   // the MLA kernels' error word (mla_decode.cu)
+}
 
 constexpr int kRecMaxK = 256;    // recurrent kernel: K <= 256, any V
 constexpr int kSimtMaxK = 256;   // SIMT chunkwise kernel: K <= 256, any V

@@ -1,0 +1,565 @@
+// mla_decode.cu -- single-token MLA decode over a static latent buffer (sm_100a).
+//
+// Drop-in for the attention core of MLA._decode_step_static
+// (kimi_linear/mla.py:117-181), NoPE (qk_rope_head_dim = 0): with
+// W = kv_b_proj.weight viewed [H, DN + DV, KVL] (W_nope = rows < DN, W_v the rest)
+//   kv_buf[b, pos] = c_kv[b]                                      (index_copy_)
+//   q_lat[b, h]    = q_nope[b, h] W_nope[h]                       (fp32)
+//   score[b, h, s] = scale * q_lat[b, h] . kv_buf[b, s],  s <= pos, else -inf
+//   p              = softmax_s(score)                             (fp32)
+//   mixed[b, h]    = sum_s p kv_buf[b, s]      (p and the result in kv_buf's dtype)
+//   out[b, h]      = mixed[b, h] W_v[h]^T                         (fp32, then I/O dtype)
+//   pos           += 1
+// Three kernels on the caller's stream, all reading `pos` from device memory
+// (graph-capturable):
+//  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, b)); CTA (0, b) also
+//    writes the new latent row at pos;
+//  * mla_attn_kernel: flash decoding.  One CTA per (split, b) walks 64-position
+//    tiles of kv_buf[b] (tiles past pos are not loaded), two TMA stages with a
+//    128-byte swizzle.  Scores: f16/bf16 mma.sync with q_lat split into hi + lo
+//    parts (fp32-level scores against exact buffer values), K split over the
+//    four warps and summed in shared memory; online softmax in fp32; mixing
+//    P . tile with N split over the warps.  Writes (max, sum, acc) partials;
+//  * mla_combine_kernel: merges the partials per (h, b), rounds mixed to the
+//    buffer dtype as the reference does, projects with W_v in fp32 and
+//    advances pos.
+#include <cuda.h>
+#include <cstring>
+#include <type_traits>
+
+#include "kda_internal.cuh"
+#include "tc_ptx.cuh"
+
+namespace kda {
+namespace mla {
+
+// this file's device error word (device variables are per translation unit
+// without relocatable device code); kda_device_error() reports it too
+__device__ int g_mla_device_error = 0;
+
+constexpr int TS = 64;            // positions per tile
+constexpr int NW = 4;             // warps per attention CTA
+constexpr int HM = 16;            // heads per CTA (MMA M); H <= 16
+constexpr int PP = TS * 2 + 16;   // pitch of P [16][64] in bytes (conflict-free ldmatrix)
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr int kMaxSplits = 256;   // splits of the position range per batch row
+
+template <typename T> struct MmaT;
+template <> struct MmaT<__half> {
+  static __device__ __forceinline__ void mma(float* d, const uint32_t* a, const uint32_t* b) {
+    ptx::mma_f16_16x8x16(d, a, b);
+  }
+  static __device__ __forceinline__ uint32_t pack(float x, float y) {
+    const __half2 h = __floats2half2_rn(x, y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack(uint32_t u) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+  }
+};
+template <> struct MmaT<__nv_bfloat16> {
+  static __device__ __forceinline__ void mma(float* d, const uint32_t* a, const uint32_t* b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  }
+  static __device__ __forceinline__ uint32_t pack(float x, float y) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ float2 unpack(uint32_t u) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+  }
+};
+
+// x = hi + lo with hi, lo in T (pairs packed): hi carries the leading bits,
+// lo the residual, so hi . b + lo . b is the fp32 product to ~2^-17 relative
+template <typename T>
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  hi = MmaT<T>::pack(x, y);
+  const float2 h = MmaT<T>::unpack(hi);
+  lo = MmaT<T>::pack(x - h.x, y - h.y);
+}
+
+// byte offset of (row s, 16-byte chunk j) of a tile of 64-channel boxes
+// (TMA SWIZZLE_128B: 128-byte rows, chunk index xor row % 8)
+__device__ __forceinline__ int swz(int group, int s, int j) {
+  return group * (TS * 128) + s * 128 + ((j ^ (s & 7)) << 4);
+}
+
+struct MlaParams {
+  int B, L, H, KVL, DN, DV;
+  float scale;
+  const void* q_nope; int64_t q_s[3];
+  const void* c_kv; int64_t c_s[2];
+  void* kv_buf; int64_t kv_s[3];
+  int64_t* pos;
+  const void* w; int64_t w_s[2];
+  void* out; int64_t o_s[3];
+  float* qlat;      // [B][16][KVL] fp32 (heads >= H zero)
+  float* part;      // [B][nsplit][16][KVL + 2]: acc, then max and sum
+  int nsplit, tiles_per_cta;
+};
+
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256)
+mla_qlat_kernel(const MlaParams p) {
+  extern __shared__ float qs[];                       // q_nope[b, h] (DN fp32)
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  float* ql = p.qlat + ((size_t)b * HM + h) * p.KVL;
+  if (h >= p.H) {                                     // padded head rows: zero
+    for (int c = tid; c < p.KVL; c += blockDim.x) ql[c] = 0.f;
+    return;
+  }
+  const T* qn = static_cast<const T*>(p.q_nope) + b * p.q_s[0] + h * p.q_s[1];
+  for (int d = tid; d < p.DN; d += blockDim.x) qs[d] = ld(qn + (int64_t)d * p.q_s[2]);
+  if (h == 0) {                                       // kv_buf[b, pos] = c_kv[b]
+    const int64_t pos = *p.pos;
+    if (pos >= 0 && pos < p.L) {
+      const T* src = static_cast<const T*>(p.c_kv) + b * p.c_s[0];
+      T* dst = static_cast<T*>(p.kv_buf) + b * p.kv_s[0] + pos * p.kv_s[1];
+      for (int c = tid; c < p.KVL; c += blockDim.x) dst[c] = src[(int64_t)c * p.c_s[1]];
+    } else if (tid == 0) {
+      atomicExch(&g_mla_device_error, 4);             // position outside the buffer
+    }
+  }
+  __syncthreads();
+  const T* wb = static_cast<const T*>(p.w) + (int64_t)h * (p.DN + p.DV) * p.w_s[0];
+  for (int c = tid; c < p.KVL; c += blockDim.x) {
+    float acc = 0.f;
+    for (int d = 0; d < p.DN; ++d) acc = fmaf(qs[d], ld(wb + (int64_t)d * p.w_s[0] + c * p.w_s[1]), acc);
+    ql[c] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T, int KVL>
+struct AttnCfg {
+  static constexpr int GROUPS = KVL / 64;             // 64-channel TMA boxes per tile
+  static constexpr int TILE = TS * KVL * 2;           // bytes per stage
+  static constexpr int KW = KVL / NW;                 // score channels per warp
+  static constexpr int KSTEPS = KW / 16;
+  static constexpr int NTW = KVL / NW / 8;            // mixing n-tiles per warp
+  static constexpr int OFF_P = 2 * TILE;              // P [16][64] in T, pitch PP
+  static constexpr int OFF_RED = OFF_P + HM * PP;     // [NW][16][64] fp32 score partials
+  static constexpr int OFF_ALPHA = OFF_RED + NW * HM * TS * 4;   // [16] rescale factors
+  static constexpr int OFF_BAR = OFF_ALPHA + HM * 4;
+  static constexpr int SMEM = OFF_BAR + 64;
+  static_assert(SMEM <= 227 * 1024, "mla shared memory");
+};
+
+template <typename T, int KVL>
+__global__ void __launch_bounds__(NW * 32, 1)
+mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
+  using C = AttnCfg<T, KVL>;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  uint8_t* Ps = sm + C::OFF_P;
+  float* red = reinterpret_cast<float*>(sm + C::OFF_RED);
+  float* alpha_s = reinterpret_cast<float*>(sm + C::OFF_ALPHA);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);   // [2]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int sp = blockIdx.x, b = blockIdx.y;
+  const int ntiles = (p.L + TS - 1) / TS;
+  const int64_t pos = *p.pos;                         // valid positions: 0 .. pos
+  const int last = (int)(pos < (int64_t)p.L - 1 ? pos : (int64_t)p.L - 1);
+  const int t_beg = sp * p.tiles_per_cta;
+  const int t_end = min(min(ntiles, t_beg + p.tiles_per_cta), last / TS + 1);
+  const int lm_row = (lane & 7) + 8 * ((lane >> 3) & 1);
+  const int lm_hi = lane >> 4;
+
+  if (tid == 0) {
+    ptx::mbar_init(&full[0], 1);
+    ptx::mbar_init(&full[1], 1);
+    ptx::fence_mbar_init();
+    *abort_flag = 0;
+  }
+  __syncthreads();
+  auto fetch = [&](int t, int stage) {                // thread 0 only
+    ptx::mbar_arrive_expect_tx(&full[stage], C::TILE);
+    for (int g = 0; g < C::GROUPS; ++g)
+      ptx::tma_load_3d(sm + stage * C::TILE + g * TS * 128, &tm, 64 * g, t * TS, b, &full[stage]);
+  };
+  uint32_t pending = 0, pend_par = 0;
+  if (tid == 0) {
+    for (int i = 0; i < 2 && t_beg + i < t_end; ++i) {
+      fetch(t_beg + i, i);
+      pending |= 1u << i;
+    }
+  }
+
+  // q_lat of this warp's channel range as hi / lo A fragments
+  uint32_t ahi[C::KSTEPS][4], alo[C::KSTEPS][4];
+  {
+    const float* ql = p.qlat + (size_t)b * HM * KVL;
+#pragma unroll
+    for (int ks = 0; ks < C::KSTEPS; ++ks) {
+      const int c = warp * C::KW + 16 * ks + 2 * tig;
+      const float2 r0 = *reinterpret_cast<const float2*>(ql + gid * KVL + c);
+      const float2 r1 = *reinterpret_cast<const float2*>(ql + (gid + 8) * KVL + c);
+      const float2 r2 = *reinterpret_cast<const float2*>(ql + gid * KVL + c + 8);
+      const float2 r3 = *reinterpret_cast<const float2*>(ql + (gid + 8) * KVL + c + 8);
+      split2<T>(r0.x, r0.y, ahi[ks][0], alo[ks][0]);
+      split2<T>(r1.x, r1.y, ahi[ks][1], alo[ks][1]);
+      split2<T>(r2.x, r2.y, ahi[ks][2], alo[ks][2]);
+      split2<T>(r3.x, r3.y, ahi[ks][3], alo[ks][3]);
+    }
+  }
+  // running softmax state (threads: head tid / 8, 8 positions each) and the
+  // output accumulator (warp: channels 128 w .., rows gid and gid + 8)
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[C::NTW][4];
+#pragma unroll
+  for (int nt = 0; nt < C::NTW; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+
+  int k = 0;
+  for (int t = t_beg; t < t_end; ++t, ++k) {
+    const int stage = k & 1;
+    const uint8_t* tile = sm + stage * C::TILE;
+    if (ptx::mbar_wait(&full[stage], (k >> 1) & 1, kWaitNs)) {
+      if (tid == 0) pending &= ~(1u << stage);
+    } else {
+      *abort_flag = 1;
+    }
+    // ---- scores: this warp's KW channels, all 64 positions
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < C::KSTEPS; ++ks) {
+      const int c0 = warp * C::KW + 16 * ks;          // multiple of 16
+      const int g = c0 >> 6, j0 = (c0 & 63) >> 3;
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {                // pairs of 8-position n-tiles
+        // matrices: (rows 16np.., chunk j0), (.., j0 + 1), (rows 16np + 8.., j0), (.., j0 + 1)
+        const int s = 16 * np + (lane & 7) + 8 * lm_hi;
+        const int j = j0 + ((lane >> 3) & 1);
+        uint32_t bf[4];
+        ptx::ldmatrix_x4(bf, tile + swz(g, s, j));
+        MmaT<T>::mma(sc[2 * np], ahi[ks], bf);
+        MmaT<T>::mma(sc[2 * np], alo[ks], bf);
+        MmaT<T>::mma(sc[2 * np + 1], ahi[ks], bf + 2);
+        MmaT<T>::mma(sc[2 * np + 1], alo[ks], bf + 2);
+      }
+    }
+    {
+      float* rw = red + warp * HM * TS;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int s = 8 * nt + 2 * tig;
+        *reinterpret_cast<float2*>(rw + gid * TS + s) = make_float2(sc[nt][0], sc[nt][1]);
+        *reinterpret_cast<float2*>(rw + (gid + 8) * TS + s) = make_float2(sc[nt][2], sc[nt][3]);
+      }
+    }
+    __syncthreads();
+    if (*abort_flag) break;
+    // ---- online softmax: thread -> head hh, positions 8 q .. 8 q + 7
+    {
+      const int hh = tid >> 3, q = tid & 7;
+      float v[8];
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int s = 8 * q + i;
+        float x = red[hh * TS + s] + red[HM * TS + hh * TS + s] + red[2 * HM * TS + hh * TS + s] +
+                  red[3 * HM * TS + hh * TS + s];
+        x *= p.scale;
+        if ((int64_t)t * TS + s > last || hh >= p.H) x = -INFINITY;
+        v[i] = x;
+        mt = fmaxf(mt, x);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float m_new = fmaxf(m_run, mt);
+      const float a = (m_new == -INFINITY) ? 1.f : expf(m_run - m_new);
+      float ls = 0.f;
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const float e0 = (v[i] == -INFINITY) ? 0.f : expf(v[i] - m_new);
+        const float e1 = (v[i + 1] == -INFINITY) ? 0.f : expf(v[i + 1] - m_new);
+        ls += e0 + e1;
+        pk[i / 2] = MmaT<T>::pack(e0, e1);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      l_run = l_run * a + ls;
+      m_run = m_new;
+      *reinterpret_cast<uint4*>(Ps + hh * PP + 16 * q) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      if (q == 0) alpha_s[hh] = a;
+    }
+    __syncthreads();
+    // ---- acc = alpha acc + P . tile for this warp's channels
+    {
+      const float a0 = alpha_s[gid], a1 = alpha_s[gid + 8];
+#pragma unroll
+      for (int nt = 0; nt < C::NTW; ++nt) {
+        acc[nt][0] *= a0; acc[nt][1] *= a0;
+        acc[nt][2] *= a1; acc[nt][3] *= a1;
+      }
+#pragma unroll
+      for (int ks = 0; ks < TS / 16; ++ks) {
+        uint32_t af[4];
+        ptx::ldmatrix_x4(af, Ps + lm_row * PP + (16 * ks + 8 * lm_hi) * 2);
+#pragma unroll
+        for (int np = 0; np < C::NTW / 2; ++np) {
+          // B[k = s][n = c]: rows s, transposed; matrices (s 16ks.., c 16np'..),
+          // (s 16ks + 8.., same c), (s 16ks.., c + 8), (s 16ks + 8.., c + 8)
+          const int c0 = warp * (KVL / NW) + 16 * np;
+          const int g = c0 >> 6, j = ((c0 & 63) >> 3) + lm_hi;
+          const int s = 16 * ks + (lane & 7) + 8 * ((lane >> 3) & 1);
+          uint32_t bf[4];
+          ptx::ldmatrix_x4_trans(bf, tile + swz(g, s, j));
+          MmaT<T>::mma(acc[2 * np], af, bf);
+          MmaT<T>::mma(acc[2 * np + 1], af, bf + 2);
+        }
+      }
+    }
+    __syncthreads();                                  // stage, P and red free
+    if (tid == 0 && t + 2 < t_end) {
+      ptx::fence_proxy_async_smem();
+      fetch(t + 2, stage);
+      pending |= 1u << stage;
+      pend_par = (pend_par & ~(1u << stage)) | ((((k + 2) >> 1) & 1u) << stage);
+    }
+  }
+
+  if (*abort_flag) {
+    if (tid == 0) {
+      atomicExch(&g_mla_device_error, 5);
+      for (int st = 0; st < 2; ++st)
+        if (pending & (1u << st)) ptx::mbar_wait(&full[st], (pend_par >> st) & 1u, kWaitNs / 2);
+    }
+    return;
+  }
+  // partials: acc rows (heads) gid, gid + 8; then max and sum per head
+  float* pb = p.part + (((size_t)b * p.nsplit + sp) * HM) * (KVL + 2);
+#pragma unroll
+  for (int nt = 0; nt < C::NTW; ++nt) {
+    const int c = warp * (KVL / NW) + 8 * nt + 2 * tig;
+    *reinterpret_cast<float2*>(pb + gid * (KVL + 2) + c) = make_float2(acc[nt][0], acc[nt][1]);
+    *reinterpret_cast<float2*>(pb + (gid + 8) * (KVL + 2) + c) = make_float2(acc[nt][2], acc[nt][3]);
+  }
+  if ((tid & 7) == 0) {
+    const int hh = tid >> 3;
+    pb[hh * (KVL + 2) + KVL] = m_run;
+    pb[hh * (KVL + 2) + KVL + 1] = l_run;
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256)
+mla_combine_kernel(const MlaParams p) {
+  extern __shared__ float mixed[];                    // [KVL] fp32 (rounded to T)
+  __shared__ float wsc[kMaxSplits];
+  __shared__ float tot;
+  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int KVL = p.KVL, ns = p.nsplit;
+  const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
+  const size_t sstride = (size_t)HM * (KVL + 2);
+  if (tid == 0) {
+    float M = -INFINITY;
+    for (int i = 0; i < ns; ++i) M = fmaxf(M, pb[i * sstride + KVL]);
+    float Lsum = 0.f;
+    for (int i = 0; i < ns; ++i) {
+      const float mi = pb[i * sstride + KVL];
+      const float w = (mi == -INFINITY) ? 0.f : expf(mi - M);
+      wsc[i] = w;
+      Lsum += w * pb[i * sstride + KVL + 1];
+    }
+    tot = Lsum;
+  }
+  __syncthreads();
+  const float inv = tot > 0.f ? 1.f / tot : 0.f;
+  for (int c = tid; c < KVL; c += blockDim.x) {
+    float x = 0.f;
+    for (int i = 0; i < ns; ++i) x = fmaf(wsc[i], pb[i * sstride + c], x);
+    const T r = static_cast<T>(x * inv);              // mixed in the buffer dtype
+    mixed[c] = static_cast<float>(r);
+  }
+  __syncthreads();
+  // out[b, h, d] = mixed . W_v[h, d]: a warp per output row, lanes over channels
+  const T* wv = static_cast<const T*>(p.w) + ((int64_t)h * (p.DN + p.DV) + p.DN) * p.w_s[0];
+  T* ob = static_cast<T*>(p.out) + b * p.o_s[0] + h * p.o_s[1];
+  for (int d = warp; d < p.DV; d += blockDim.x / 32) {
+    const T* wr = wv + (int64_t)d * p.w_s[0];
+    float s = 0.f;
+    for (int c = lane; c < KVL; c += 32) s = fmaf(mixed[c], ld(wr + (int64_t)c * p.w_s[1]), s);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) st(ob + (int64_t)d * p.o_s[2], s);
+  }
+  if (h == 0 && b == 0 && tid == 0) {
+    // every CTA has read what it needs of pos (the attention kernel is done)
+    *p.pos += 1;
+  }
+}
+
+}  // namespace mla
+}  // namespace kda
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace kda {
+namespace mla {
+namespace {
+
+// positions split over CTAs: about one CTA per SM over all batch rows
+void plan(int B, int L, int num_sms, int* nsplit, int* tpc) {
+  const int ntiles = (L + TS - 1) / TS;
+  int t = (int)(((long)ntiles * B + num_sms - 1) / num_sms);
+  t = max(t, 1);
+  int n = (ntiles + t - 1) / t;
+  if (n > kMaxSplits) {
+    t = (ntiles + kMaxSplits - 1) / kMaxSplits;
+    n = (ntiles + t - 1) / t;
+  }
+  *nsplit = n;
+  *tpc = t;
+}
+
+int device_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+size_t ws_bytes(int B, int L, int KVL) {
+  int ns, tpc;
+  plan(B, L, device_sms(), &ns, &tpc);
+  const size_t qlat = (size_t)B * HM * KVL * 4;
+  const size_t part = (size_t)B * ns * HM * (KVL + 2) * 4;
+  return ((qlat + 255) / 256) * 256 + part;
+}
+
+bool kvl_ok(int kvl) { return kvl == 64 || kvl == 128 || kvl == 256 || kvl == 512; }
+
+int validate(const MlaDecodeArgs* a) {
+  if (a == nullptr) return KDA_ERR_NULL_POINTER;
+  if (a->abi_version != KDA_B200_ABI_VERSION) return KDA_ERR_SHAPE;
+  if (a->B < 1 || a->L < 1 || a->H < 1 || a->H > HM || !kvl_ok(a->KVL) || a->DN < 1 ||
+      a->DV < 1 || a->B > 65535)
+    return KDA_ERR_SHAPE;
+  if (a->io_dtype != KDA_DTYPE_F16 && a->io_dtype != KDA_DTYPE_BF16) return KDA_ERR_DTYPE;
+  if (!a->q_nope || !a->c_kv || !a->kv_buf || !a->pos || !a->w || !a->out || !a->workspace)
+    return KDA_ERR_NULL_POINTER;
+  // kv_buf goes through a tensor map: unit channel stride, 16-byte rows
+  if (a->kv_buf_stride[2] != 1) return KDA_ERR_STRIDE;
+  if (reinterpret_cast<uintptr_t>(a->kv_buf) % 16 || (a->kv_buf_stride[0] * 2) % 16 ||
+      (a->kv_buf_stride[1] * 2) % 16 || a->kv_buf_stride[0] <= 0 || a->kv_buf_stride[1] <= 0)
+    return KDA_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(a->workspace) % 256 ||
+      reinterpret_cast<uintptr_t>(a->pos) % 8)
+    return KDA_ERR_ALIGNMENT;
+  if (a->workspace_bytes < ws_bytes(a->B, a->L, a->KVL)) return KDA_ERR_WORKSPACE;
+  return KDA_OK;
+}
+
+template <typename T, int KVL>
+cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
+  auto k = mla_attn_kernel<T, KVL>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       AttnCfg<T, KVL>::SMEM);
+  if (e != cudaSuccess) return e;
+  k<<<dim3(p.nsplit, p.B), NW * 32, AttnCfg<T, KVL>::SMEM, s>>>(p, tm);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
+  mla_qlat_kernel<T><<<dim3(HM, p.B), 256, p.DN * sizeof(float), s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  switch (p.KVL) {
+    case 64: e = launch_attn<T, 64>(p, tm, s); break;
+    case 128: e = launch_attn<T, 128>(p, tm, s); break;
+    case 256: e = launch_attn<T, 256>(p, tm, s); break;
+    default: e = launch_attn<T, 512>(p, tm, s); break;
+  }
+  if (e != cudaSuccess) return e;
+  mla_combine_kernel<T><<<dim3(p.H, p.B), 256, p.KVL * sizeof(float), s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int read_device_error(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_mla_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v != 0) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_mla_device_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
+}  // namespace mla
+}  // namespace kda
+
+extern "C" {
+
+size_t mla_decode_workspace_bytes(const MlaDecodeArgs* a) {
+  if (a == nullptr || a->B < 1 || a->L < 1 || !kda::mla::kvl_ok(a->KVL)) return 0;
+  return kda::mla::ws_bytes(a->B, a->L, a->KVL);
+}
+
+size_t mla_decode_args_size(void) { return sizeof(MlaDecodeArgs); }
+
+int mla_decode_fwd(const MlaDecodeArgs* a, void* stream) {
+  using namespace kda;
+  using namespace kda::mla;
+  int st = validate(a);
+  if (st != KDA_OK) return st;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return KDA_ERR_LAUNCH;
+  if (major != 10) return KDA_ERR_ARCH;
+  MlaParams p{};
+  p.B = a->B; p.L = a->L; p.H = a->H; p.KVL = a->KVL; p.DN = a->DN; p.DV = a->DV;
+  p.scale = a->scale;
+  p.q_nope = a->q_nope; std::memcpy(p.q_s, a->q_nope_stride, sizeof(p.q_s));
+  p.c_kv = a->c_kv; std::memcpy(p.c_s, a->c_kv_stride, sizeof(p.c_s));
+  p.kv_buf = a->kv_buf; std::memcpy(p.kv_s, a->kv_buf_stride, sizeof(p.kv_s));
+  p.pos = a->pos;
+  p.w = a->w; std::memcpy(p.w_s, a->w_stride, sizeof(p.w_s));
+  p.out = a->out; std::memcpy(p.o_s, a->out_stride, sizeof(p.o_s));
+  plan(p.B, p.L, device_sms(), &p.nsplit, &p.tiles_per_cta);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  const size_t qlat = (size_t)p.B * HM * p.KVL * 4;
+  p.qlat = reinterpret_cast<float*>(ws);
+  p.part = reinterpret_cast<float*>(ws + ((qlat + 255) / 256) * 256);
+  // kv_buf [B, L, KVL] as a 3-D tensor map: boxes of 64 channels x 64 positions
+  EncodeTiled enc = encode_tiled();
+  if (enc == nullptr) return KDA_ERR_LAUNCH;
+  CUtensorMap tm;
+  const cuuint64_t dims[3] = {(cuuint64_t)p.KVL, (cuuint64_t)p.L, (cuuint64_t)p.B};
+  const cuuint64_t strides[2] = {(cuuint64_t)(p.kv_s[1] * 2), (cuuint64_t)(p.kv_s[0] * 2)};
+  const cuuint32_t box[3] = {64u, (cuuint32_t)TS, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType dt = a->io_dtype == KDA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (enc(&tm, dt, 3, a->kv_buf, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return KDA_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = a->io_dtype == KDA_DTYPE_F16 ? launch_all<__half>(p, tm, s)
+                                               : launch_all<__nv_bfloat16>(p, tm, s);
+  return e == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+}  // extern "C"

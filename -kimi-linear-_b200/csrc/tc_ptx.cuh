@@ -85,6 +85,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, in
       "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst_smem)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
 // L2 prefetch of one box described by a tensor map (no shared memory involved)
 __device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int c0, int c1, int c2,
                                                 int c3) {

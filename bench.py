@@ -21,6 +21,10 @@ Reported, all on the device with CUDA events on the launching stream:
                 fp32 [64,16,128,128] states, captured in a CUDA graph (four
                 steps on four distinct states: working set 4x L2) and
                 replayed, against HBM bandwidth;
+* ``mla_decode`` the MLA layer's static-buffer decode step of BASELINE
+                configs[4] (B=4, buffer 8192 + 256 latents), CUDA graph,
+                against HBM bandwidth (the rest of configs[4], the model
+                around it, cannot run on the GPU box: see DESIGN.md);
 * ``long_context`` BASELINE configs[3]: B=8, T=32768 bf16 prefill with a
                 fp32 S0, (b, h) sharded over the ranks (strong scaling), with
                 and without the final gather of o and S to rank 0;
@@ -347,6 +351,68 @@ def bench_decode(torch, kb, dev, steps, warmup, clk):
     return ms, reps * NBUF
 
 
+# MLA layer of configs[4] (1.5B hybrid, kimi_linear_1p5b_dense.json full_attn):
+# prefill B=4 x T=8192, then decode into a buffer of 8192 + 256 latents
+CFG4_MLA = dict(B=4, L=8192 + 256, H=16, KVL=512, DN=128, DV=128, prompt=8192)
+
+
+def bench_mla_decode(torch, kb, dev, steps, warmup, clk):
+    """configs[4]'s MLA decode step (static latent buffer, what GraphedDecoder
+    runs per MLA layer): the core of ``MLA._decode_step_static`` through
+    ``mla.mla_decode_core``, captured in a CUDA graph of NBUF steps on NBUF
+    distinct buffers (4 x 34.6 MB > L2), replayed.  The buffers start with the
+    8192-token prompt; every replay advances each buffer's pos by one.
+    Returns (ms per step, steps timed, algorithmic bytes per step)."""
+    NBUF = 4
+    c = CFG4_MLA
+    B, L, H, KVL, DN, DV, P = c["B"], c["L"], c["H"], c["KVL"], c["DN"], c["DV"], c["prompt"]
+    reps = max(1, min(steps // NBUF, (L - P) // NBUF - warmup - 2))
+    g = torch.Generator(device=dev).manual_seed(11)
+    f16 = dict(device=dev, dtype=torch.float16)
+    w = torch.randn(H * (DN + DV), KVL, generator=g, device=dev).mul_(KVL ** -0.5).half()
+    q = torch.randn(B, 1, H, DN, generator=g, device=dev).mul_(0.5).half()
+    ck = torch.randn(B, 1, KVL, generator=g, device=dev).half()
+    bufs, poss = [], []
+    for _ in range(NBUF):
+        b = torch.zeros(B, L, KVL, **f16)
+        b[:, :P].copy_(torch.randn(B, P, KVL, generator=g, device=dev))
+        bufs.append(b)
+        poss.append(torch.tensor([P], dtype=torch.int64, device=dev))
+    scale = DN ** -0.5
+
+    def steps_all():
+        return [kb.mla.mla_decode_core(q, ck, bufs[i], poss[i], w, H, DN, DV, scale)
+                for i in range(NBUF)]
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        steps_all()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        steps_all()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    pos_mid = int(poss[0].item())
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    clk.start()
+    for i in range(reps):
+        starts[i].record()
+        graph.replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    clk.stop()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / (reps * NBUF)
+    del graph
+    # bytes a step must move: the valid latent rows, kv_b_proj.weight, q, c_kv, out
+    valid = pos_mid + reps // 2 + 1
+    nbytes = B * valid * KVL * 2 + H * (DN + DV) * KVL * 2 + B * H * (DN + DV) * 2 + B * KVL * 2
+    return ms, reps * NBUF, nbytes
+
+
 def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
     """Config 3: B=8, T=32768, H=16 bf16 prefill with a fp32 S0, (b, h)
     sharded over the ranks (strong scaling), then o and S gathered to rank 0.
@@ -442,6 +508,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=1024)
     ap.add_argument("--long-steps", type=int, default=4,
                     help="timed steps of the configs[3] leg (0 skips it)")
+    ap.add_argument("--mla-steps", type=int, default=128,
+                    help="timed steps of the configs[4] MLA decode leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=("prefill", "decode"),
                     help="profiling target: run the workload three times, print nothing timed")
@@ -499,6 +567,8 @@ def main():
         if dist is not None:
             dist.all_reduce(dec_t, op=dist.ReduceOp.MAX)
         dec_ms = dec_t.item()
+        mla_ms, mla_steps, mla_bytes = bench_mla_decode(torch, kb, dev, a.mla_steps, a.warmup,
+                                                        clk)
         long_ctx = None
         if a.long_steps > 0:
             long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, dist, world,
@@ -560,6 +630,18 @@ def main():
                                     "frac": dec_bytes / (dec_ms * 1e-3) / 1e9 / hbm,
                                     "traffic": _traffic("kda_recurrent", "cfg2"),
                                     "algorithmic_bytes": dec_bytes}},
+            "mla_decode": {"workload": "MLA static-buffer decode step of configs[4] "
+                                       "(B=4, 16 heads, kv_lora_rank 512, head dims 128, "
+                                       "buffer 8192 + 256 latents, fp16)",
+                           "value": world * CFG4_MLA["B"] / (mla_ms * 1e-3), "unit": "tokens/s",
+                           "ms_per_step": mla_ms, "steps": mla_steps,
+                           "timing": "CUDA graph of 4 steps on 4 distinct 34.6 MB buffers, "
+                                     "replayed; device time per step",
+                           "roofline": {"bound": "hbm",
+                                        "achieved": mla_bytes / (mla_ms * 1e-3) / 1e9,
+                                        "peak": hbm, "unit": "GB/s",
+                                        "frac": mla_bytes / (mla_ms * 1e-3) / 1e9 / hbm,
+                                        "algorithmic_bytes": mla_bytes}},
             "long_context": long_ctx,
             "gpu_launches": a.steps * launches_per_call,
             "clocks": clocks,

@@ -6,6 +6,11 @@
  *   kda_chunkwise_fwd  replaces kimi_linear/kda.py:58-185 (kda_chunkwise)
  *   kda_recurrent_fwd  replaces kimi_linear/kda.py:188-219 (kda_recurrent)
  *
+ * and, around it, the fused prologue / epilogue of the KDA block
+ * (kda_prologue_fwd, kda_epilogue_fwd), the gradient of the core
+ * (kda_backward) and the static-buffer MLA decode step of the full-attention
+ * layers (mla_decode_fwd, kimi_linear/mla.py:117-181).
+ *
  * Plain pointers, sizes and element strides only.  The Python host layer
  * (-kimi-linear-_b200/ops.py) keeps the reference's Python signatures and
  * calls these entry points through ctypes; any other FFI can bind them the
@@ -144,8 +149,9 @@ int kda_device_supported(int device);
 
 /*
  * Error word written by a kernel that abandoned its work after a bounded wait
- * on the GPU ran out (0 = none); clear != 0 resets it.  Synchronises with the
- * device.  <0 on a CUDA error.  No reference counterpart (diagnostic).
+ * on the GPU ran out, or (MLA decode) found pos outside the buffer (0 = none);
+ * clear != 0 resets it.  Synchronises with the device.  <0 on a CUDA error.
+ * No reference counterpart (diagnostic).
  */
 int kda_device_error(int clear);
 
@@ -275,6 +281,44 @@ size_t kda_backward_args_size(void);
 /* sizeof(KdaPrologueArgs) / sizeof(KdaEpilogueArgs) as compiled. */
 size_t kda_prologue_args_size(void);
 size_t kda_epilogue_args_size(void);
+
+/*
+ * Single-token MLA decode over a static latent buffer: the attention core of
+ * MLA._decode_step_static (kimi_linear/mla.py:117-181) for NoPE layers
+ * (qk_rope_head_dim == 0), everything between the projections and o_proj:
+ *   kv_buf[b, pos] = c_kv[b]; q_lat = q_nope W_nope (fp32);
+ *   p = softmax(scale q_lat kv_buf[b, :pos+1]^T) (fp32, positions > pos masked);
+ *   mixed = p kv_buf (kv_buf's dtype); out = mixed W_v^T (fp32 -> io dtype);
+ *   pos += 1.
+ * pos is read and advanced in device memory (capturable in a CUDA graph).
+ *   q_nope : [B, H, DN]      c_kv : [B, KVL]        (io dtype, any strides)
+ *   kv_buf : [B, L, KVL]     io dtype, unit channel stride, 16-byte rows
+ *   pos    : int64[1] device memory
+ *   w      : kv_b_proj.weight [H*(DN+DV), KVL]       (io dtype)
+ *   out    : [B, H, DV]      io dtype
+ * Requires io dtype f16 or bf16, H <= 16, KVL in {64, 128, 256, 512}.
+ */
+typedef struct MlaDecodeArgs {
+  int32_t abi_version;
+  int32_t B, L, H, KVL, DN, DV;
+  int32_t io_dtype;
+  float scale;                 /* (DN + qk_rope_head_dim)^-0.5 in the reference */
+  const void* q_nope; int64_t q_nope_stride[3];
+  const void* c_kv;   int64_t c_kv_stride[2];
+  void* kv_buf;       int64_t kv_buf_stride[3];
+  int64_t* pos;
+  const void* w;      int64_t w_stride[2];
+  void* out;          int64_t out_stride[3];
+  void* workspace;    size_t workspace_bytes;   /* mla_decode_workspace_bytes(), 256-byte aligned */
+} MlaDecodeArgs;
+
+int mla_decode_fwd(const MlaDecodeArgs* args, void* stream);
+
+/* device workspace of mla_decode_fwd for these B, L, KVL (0 for invalid sizes). */
+size_t mla_decode_workspace_bytes(const MlaDecodeArgs* args);
+
+/* sizeof(MlaDecodeArgs) as compiled. */
+size_t mla_decode_args_size(void);
 
 /* sizeof(KdaArgs) as compiled, for FFI layout checks. */
 size_t kda_args_size(void);

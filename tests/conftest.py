@@ -33,7 +33,24 @@ def pkg():
 def golden_cases():
     """Golden cases of the KDA core (tests/golden/make_golden.py)."""
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
-                  if not os.path.basename(p).startswith(("fused_", "grad_")))
+                  if not os.path.basename(p).startswith(("fused_", "grad_", "mla_")))
+
+
+def mla_cases():
+    """Golden static-buffer MLA decode steps (tests/golden/make_golden_mla.py)."""
+    return sorted(os.path.basename(p)[:-4]
+                  for p in glob.glob(os.path.join(GOLDEN, "mla_*.npz")))
+
+
+def load_mla(name):
+    """Golden MLA case ``name``: arrays plus B, L, H, KVL, DN, DV, hidden, pos,
+    pos_after, dtype (string) and scale."""
+    z = np.load(os.path.join(GOLDEN, f"{name}.npz"))
+    d = {k: z[k] for k in z.files}
+    B, L, H, KVL, DN, DV, hidden, pos, pos_after = (int(x) for x in d["meta"])
+    d.update(B=B, L=L, H=H, KVL=KVL, DN=DN, DV=DV, hidden=hidden, pos=pos,
+             pos_after=pos_after, dtype=str(d["dtype"]), scale=float(d["scale"]))
+    return d
 
 
 def grad_cases():

@@ -18,7 +18,8 @@ HEADER = os.path.join(REPO, "include", "kda_b200.h")
 def _declared_functions():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(kda_\w+)\s*\(", src, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b((?:kda|mla)_\w+)\s*\(", src,
+                                 flags=re.M)))
 
 
 @pytest.fixture(scope="module")
@@ -39,6 +40,8 @@ def test_library_exports_every_declared_symbol(lib):
 def test_struct_layout_matches(lib):
     L = pkg()._lib
     assert lib.kda_args_size() == ctypes.sizeof(L.KdaArgs)
+    assert lib.mla_decode_args_size() == ctypes.sizeof(L.MlaDecodeArgs)
+    assert lib.kda_backward_args_size() == ctypes.sizeof(L.KdaBackwardArgs)
     assert lib.kda_abi_version() == L.ABI_VERSION
 
 
@@ -104,3 +107,40 @@ def test_path_selection_queries_need_no_device(lib):
     a = _args()
     assert lib.kda_chunkwise_path(ctypes.byref(a)) in (0, 1)
     assert lib.kda_chunkwise_path(ctypes.byref(_args(T=100))) == -pkg()._lib.KDA_ERR_CHUNK
+
+
+def _mla_args(**kw):
+    L = pkg()._lib
+    a = L.MlaDecodeArgs()
+    a.abi_version = L.ABI_VERSION
+    a.B, a.L, a.H, a.KVL, a.DN, a.DV = 2, 128, 16, 512, 128, 128
+    a.io_dtype = L.DTYPE_F16
+    a.scale = 128 ** -0.5
+    fake = 1 << 20                       # aligned non-null addresses; validation only
+    a.q_nope = a.c_kv = a.kv_buf = a.w = a.out = a.pos = a.workspace = fake
+    a.q_nope_stride = (ctypes.c_int64 * 3)(16 * 128, 128, 1)
+    a.c_kv_stride = (ctypes.c_int64 * 2)(512, 1)
+    a.kv_buf_stride = (ctypes.c_int64 * 3)(128 * 512, 512, 1)
+    a.w_stride = (ctypes.c_int64 * 2)(512, 1)
+    a.out_stride = (ctypes.c_int64 * 3)(16 * 128, 128, 1)
+    a.workspace_bytes = 0
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_mla_argument_errors_before_any_launch(lib):
+    """Argument errors come back as status codes before anything touches the GPU."""
+    L = pkg()._lib
+    call = lambda a: lib.mla_decode_fwd(ctypes.byref(a), None)  # noqa: E731
+    assert call(_mla_args(H=17)) == L.KDA_ERR_SHAPE
+    assert call(_mla_args(KVL=96)) == L.KDA_ERR_SHAPE
+    assert call(_mla_args(io_dtype=L.DTYPE_F32)) == L.KDA_ERR_DTYPE
+    assert call(_mla_args(kv_buf=None)) == L.KDA_ERR_NULL_POINTER
+    assert call(_mla_args(kv_buf_stride=(ctypes.c_int64 * 3)(128 * 512, 512, 2))) == \
+        L.KDA_ERR_STRIDE
+    assert call(_mla_args(kv_buf_stride=(ctypes.c_int64 * 3)(128 * 513, 513, 1))) == \
+        L.KDA_ERR_ALIGNMENT
+    assert call(_mla_args()) == L.KDA_ERR_WORKSPACE     # workspace_bytes = 0
+    assert lib.mla_decode_workspace_bytes(ctypes.byref(_mla_args())) > 0
+    assert lib.mla_decode_workspace_bytes(ctypes.byref(_mla_args(KVL=96))) == 0

@@ -172,3 +172,36 @@ def test_fused_cpu_tensors_raise():
     x = torch.zeros(1, 4, 64)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         kb.kda_epilogue(torch.zeros(1, 4, 2, 32), x, torch.ones(2, 32), 1e-6)
+
+
+def test_mla_decode_host_checks():
+    """The MLA decode drop-in: no CPU path, NoPE only, single token only."""
+    kb = pkg()
+    B, L, H, KVL, DN, DV = 1, 64, 4, 64, 16, 16
+    q = torch.zeros(B, 1, H, DN, dtype=torch.float16)
+    ck = torch.zeros(B, 1, KVL, dtype=torch.float16)
+    buf = torch.zeros(B, L, KVL, dtype=torch.float16)
+    pos = torch.tensor([3], dtype=torch.int64)
+    w = torch.zeros(H * (DN + DV), KVL, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="CUDA tensors"):
+        kb.mla.mla_decode_core(q, ck, buf, pos, w, H, DN, DV, DN ** -0.5)
+    m = types.SimpleNamespace(num_heads=H, qk_nope_head_dim=DN, qk_rope_head_dim=8,
+                              v_head_dim=DV, scale=0.1)
+    state = {"c_kv_buf": buf, "pos": pos}
+    with pytest.raises(NotImplementedError, match="NoPE"):
+        kb.mla.decode_step_static(m, torch.zeros(B, 1, 8), q, None, ck, None, state, True)
+    with pytest.raises(RuntimeError, match="single-token"):
+        kb.mla.decode_step_static(m, torch.zeros(B, 2, 8), q, None, ck, None, state, True)
+
+
+def test_install_mla_patches_and_restores():
+    kb = pkg()
+
+    class FakeMLA:
+        def _decode_step_static(self, *a):
+            return "reference"
+
+    kb.mla.install_mla(FakeMLA)
+    assert FakeMLA._decode_step_static is kb.mla.decode_step_static
+    kb.mla.uninstall_mla()
+    assert FakeMLA()._decode_step_static() == "reference"

@@ -101,37 +101,113 @@ struct MlaParams {
   float* qlat;      // [B][16][KVL] fp32 (heads >= H zero)
   float* part;      // [B][nsplit][16][KVL + 2]: acc, then max and sum
   int nsplit, tiles_per_cta;
+  bool w_vec;       // kv_b_proj.weight rows are 16-byte-aligned unit-stride ranges
 };
 
+// w[row, c .. c + 7] as fp32 (one 16-byte load when p.w_vec)
+template <typename T>
+__device__ __forceinline__ void ld8(const MlaParams& p, const T* w, int64_t row, int c,
+                                    float (&x)[8]) {
+  const T* r = w + row * p.w_s[0];
+  if (p.w_vec) {
+    const uint4 u = *reinterpret_cast<const uint4*>(r + c);
+    const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = MmaT<T>::unpack(v[i]);
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = ld(r + (int64_t)(c + i) * p.w_s[1]);
+  }
+}
+
 // ---------------------------------------------------------------------------
+// One CTA per (head, 128-channel slab): reads its slab of W_nope once for all
+// batch rows.  Thread t: 8-channel chunk t % 16 of the slab, rows d = t / 16,
+// t / 16 + 16, ...; the 16 row-partials meet in shared memory.
+constexpr int QL_COLS = 128;      // channels per CTA
+constexpr int QL_BB = 4;          // batch rows per pass
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 mla_qlat_kernel(const MlaParams p) {
-  extern __shared__ float qs[];                       // q_nope[b, h] (DN fp32)
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  float* ql = p.qlat + ((size_t)b * HM + h) * p.KVL;
-  if (h >= p.H) {                                     // padded head rows: zero
-    for (int c = tid; c < p.KVL; c += blockDim.x) ql[c] = 0.f;
-    return;
-  }
-  const T* qn = static_cast<const T*>(p.q_nope) + b * p.q_s[0] + h * p.q_s[1];
-  for (int d = tid; d < p.DN; d += blockDim.x) qs[d] = ld(qn + (int64_t)d * p.q_s[2]);
-  if (h == 0) {                                       // kv_buf[b, pos] = c_kv[b]
+  extern __shared__ float sh[];   // q_nope of QL_BB rows [QL_BB][DN], partials [16][QL_BB][128]
+  float* qs = sh;
+  float* part = sh + QL_BB * ((p.DN + 3) & ~3);
+  const int DNP = (p.DN + 3) & ~3;
+  const int h = blockIdx.x, c0 = blockIdx.y * QL_COLS, tid = threadIdx.x;
+  const int chunk = tid & 15, dsub = tid >> 4;
+  if (h == 0 && blockIdx.y == 0) {                    // kv_buf[b, pos] = c_kv[b]
     const int64_t pos = *p.pos;
     if (pos >= 0 && pos < p.L) {
-      const T* src = static_cast<const T*>(p.c_kv) + b * p.c_s[0];
-      T* dst = static_cast<T*>(p.kv_buf) + b * p.kv_s[0] + pos * p.kv_s[1];
-      for (int c = tid; c < p.KVL; c += blockDim.x) dst[c] = src[(int64_t)c * p.c_s[1]];
+      for (int b = 0; b < p.B; ++b) {
+        const T* src = static_cast<const T*>(p.c_kv) + b * p.c_s[0];
+        T* dst = static_cast<T*>(p.kv_buf) + b * p.kv_s[0] + pos * p.kv_s[1];
+        for (int c = tid; c < p.KVL; c += blockDim.x) dst[c] = src[(int64_t)c * p.c_s[1]];
+      }
     } else if (tid == 0) {
       atomicExch(&g_mla_device_error, 4);             // position outside the buffer
     }
   }
-  __syncthreads();
+  const int ncols = min(QL_COLS, p.KVL - c0);         // KVL = 64: half a slab
+  if (h >= p.H) {                                     // padded head rows: zero
+    for (int b = 0; b < p.B; ++b)
+      for (int c = tid; c < ncols; c += blockDim.x)
+        p.qlat[((size_t)b * HM + h) * p.KVL + c0 + c] = 0.f;
+    return;
+  }
   const T* wb = static_cast<const T*>(p.w) + (int64_t)h * (p.DN + p.DV) * p.w_s[0];
-  for (int c = tid; c < p.KVL; c += blockDim.x) {
-    float acc = 0.f;
-    for (int d = 0; d < p.DN; ++d) acc = fmaf(qs[d], ld(wb + (int64_t)d * p.w_s[0] + c * p.w_s[1]), acc);
-    ql[c] = acc;
+  for (int b0 = 0; b0 < p.B; b0 += QL_BB) {
+    const int nb = min(QL_BB, p.B - b0);
+    __syncthreads();                                  // qs / part free
+    for (int i = tid; i < nb * p.DN; i += blockDim.x) {
+      const int bb = i / p.DN, d = i - bb * p.DN;
+      const T* qn = static_cast<const T*>(p.q_nope) + (b0 + bb) * p.q_s[0] + h * p.q_s[1];
+      qs[bb * DNP + d] = ld(qn + (int64_t)d * p.q_s[2]);
+    }
+    __syncthreads();
+    float acc[QL_BB][8];
+#pragma unroll
+    for (int bb = 0; bb < QL_BB; ++bb)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[bb][e] = 0.f;
+    if (8 * chunk < ncols) {
+      // rows d = dsub + 16 k, four at a time: their weight loads overlap
+      for (int d0 = dsub; d0 < p.DN; d0 += 64) {
+        float x[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (d0 + 16 * u < p.DN) ld8(p, wb, d0 + 16 * u, c0 + 8 * chunk, x[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int d = d0 + 16 * u;
+          if (d >= p.DN) break;
+#pragma unroll
+          for (int bb = 0; bb < QL_BB; ++bb) {
+            const float qd = bb < nb ? qs[bb * DNP + d] : 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[bb][e] = fmaf(qd, x[u][e], acc[bb][e]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int bb = 0; bb < QL_BB; ++bb)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        part[(dsub * QL_BB + bb) * QL_COLS + 8 * chunk + e] = acc[bb][e];
+    __syncthreads();
+    for (int i = tid; i < nb * QL_COLS; i += blockDim.x) {
+      const int bb = i / QL_COLS, c = i - bb * QL_COLS;
+      if (c >= ncols) continue;
+      float x = 0.f;
+#pragma unroll
+      for (int ds = 0; ds < 16; ++ds) x += part[(ds * QL_BB + bb) * QL_COLS + c];
+      p.qlat[((size_t)(b0 + bb) * HM + h) * p.KVL + c0 + c] = x;
+    }
   }
 }
 
@@ -368,34 +444,70 @@ mla_combine_kernel(const MlaParams p) {
   const int KVL = p.KVL, ns = p.nsplit;
   const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
   const size_t sstride = (size_t)HM * (KVL + 2);
+  // split weights exp(m_i - M) and the total sum, all threads in parallel
+  __shared__ float red[8];
+  float mi = -INFINITY, li = 0.f;
+  if (tid < ns) {
+    mi = pb[tid * sstride + KVL];
+    li = pb[tid * sstride + KVL + 1];
+  }
+  float M = mi;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = red[0];
+  for (int w = 1; w < (int)(blockDim.x / 32); ++w) M = fmaxf(M, red[w]);
+  const float wi = (tid < ns && mi != -INFINITY) ? expf(mi - M) : 0.f;
+  if (tid < ns) wsc[tid] = wi;
+  float lw = wi * li;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+  __syncthreads();                                    // every thread has read red[] (max)
+  if (lane == 0) red[warp] = lw;
+  __syncthreads();
   if (tid == 0) {
-    float M = -INFINITY;
-    for (int i = 0; i < ns; ++i) M = fmaxf(M, pb[i * sstride + KVL]);
-    float Lsum = 0.f;
-    for (int i = 0; i < ns; ++i) {
-      const float mi = pb[i * sstride + KVL];
-      const float w = (mi == -INFINITY) ? 0.f : expf(mi - M);
-      wsc[i] = w;
-      Lsum += w * pb[i * sstride + KVL + 1];
-    }
-    tot = Lsum;
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += red[w];
+    tot = t;
   }
   __syncthreads();
   const float inv = tot > 0.f ? 1.f / tot : 0.f;
   for (int c = tid; c < KVL; c += blockDim.x) {
-    float x = 0.f;
-    for (int i = 0; i < ns; ++i) x = fmaf(wsc[i], pb[i * sstride + c], x);
+    // eight independent partial sums: the split loads overlap instead of
+    // waiting one after another
+    float xs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int i = 0;
+    for (; i + 8 <= ns; i += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = pb[(size_t)(i + u) * sstride + c];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) xs[u] = fmaf(wsc[i + u], v[u], xs[u]);
+    }
+    for (; i < ns; ++i) xs[0] = fmaf(wsc[i], pb[(size_t)i * sstride + c], xs[0]);
+    const float x = ((xs[0] + xs[1]) + (xs[2] + xs[3])) + ((xs[4] + xs[5]) + (xs[6] + xs[7]));
     const T r = static_cast<T>(x * inv);              // mixed in the buffer dtype
     mixed[c] = static_cast<float>(r);
   }
   __syncthreads();
-  // out[b, h, d] = mixed . W_v[h, d]: a warp per output row, lanes over channels
+  // out[b, h, d] = mixed . W_v[h, d]: warp w takes rows d = w, w + 8, ...;
+  // lanes 8-channel chunks (16-byte loads), then a warp sum
   const T* wv = static_cast<const T*>(p.w) + ((int64_t)h * (p.DN + p.DV) + p.DN) * p.w_s[0];
   T* ob = static_cast<T*>(p.out) + b * p.o_s[0] + h * p.o_s[1];
+  const int nch = KVL / 8;
   for (int d = warp; d < p.DV; d += blockDim.x / 32) {
-    const T* wr = wv + (int64_t)d * p.w_s[0];
     float s = 0.f;
-    for (int c = lane; c < KVL; c += 32) s = fmaf(mixed[c], ld(wr + (int64_t)c * p.w_s[1]), s);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int ch = lane + 32 * j;
+      if (ch < nch) {
+        float x[8];
+        ld8(p, wv, d, 8 * ch, x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s = fmaf(mixed[8 * ch + e], x[e], s);
+      }
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (lane == 0) st(ob + (int64_t)d * p.o_s[2], s);
@@ -480,7 +592,13 @@ cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t 
 
 template <typename T>
 cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
-  mla_qlat_kernel<T><<<dim3(HM, p.B), 256, p.DN * sizeof(float), s>>>(p);
+  const size_t qsm = (size_t)(QL_BB * ((p.DN + 3) & ~3) + 16 * QL_BB * QL_COLS) * sizeof(float);
+  if (qsm > 48 * 1024) {
+    cudaError_t ea = cudaFuncSetAttribute(mla_qlat_kernel<T>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
+    if (ea != cudaSuccess) return ea;
+  }
+  mla_qlat_kernel<T><<<dim3(HM, (p.KVL + QL_COLS - 1) / QL_COLS), 256, qsm, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   switch (p.KVL) {
@@ -537,6 +655,8 @@ int mla_decode_fwd(const MlaDecodeArgs* a, void* stream) {
   p.pos = a->pos;
   p.w = a->w; std::memcpy(p.w_s, a->w_stride, sizeof(p.w_s));
   p.out = a->out; std::memcpy(p.o_s, a->out_stride, sizeof(p.o_s));
+  p.w_vec = a->w_stride[1] == 1 && reinterpret_cast<uintptr_t>(a->w) % 16 == 0 &&
+            (a->w_stride[0] * 2) % 16 == 0;
   plan(p.B, p.L, device_sms(), &p.nsplit, &p.tiles_per_cta);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
   const size_t qlat = (size_t)p.B * HM * p.KVL * 4;

@@ -10,19 +10,20 @@
 //   mixed[b, h]    = sum_s p kv_buf[b, s]      (p and the result in kv_buf's dtype)
 //   out[b, h]      = mixed[b, h] W_v[h]^T                         (fp32, then I/O dtype)
 //   pos           += 1
-// Three kernels on the caller's stream, all reading `pos` from device memory
+// Four kernels on the caller's stream, reading `pos` from device memory
 // (graph-capturable):
 //  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, b)); CTA (0, b) also
 //    writes the new latent row at pos;
 //  * mla_attn_kernel: flash decoding.  One CTA per (split, b) walks 64-position
-//    tiles of kv_buf[b] (tiles past pos are not loaded), two TMA stages with a
+//    tiles of kv_buf[b] (tiles past pos are not loaded), three TMA stages with a
 //    128-byte swizzle.  Scores: f16/bf16 mma.sync with q_lat split into hi + lo
 //    parts (fp32-level scores against exact buffer values), K split over the
 //    four warps and summed in shared memory; online softmax in fp32; mixing
 //    P . tile with N split over the warps.  Writes (max, sum, acc) partials;
-//  * mla_combine_kernel: merges the partials per (h, b), rounds mixed to the
-//    buffer dtype as the reference does, projects with W_v in fp32 and
-//    advances pos.
+//  * mla_mix_kernel: merges the partials per (channel slab, h, b) and rounds
+//    mixed to the buffer dtype as the reference does;
+//  * mla_out_kernel: projects with W_v in fp32 (each W_v row read once for all
+//    batch rows) and advances pos.
 #include <cuda.h>
 #include <cstring>
 #include <type_traits>
@@ -100,6 +101,7 @@ struct MlaParams {
   void* out; int64_t o_s[3];
   float* qlat;      // [B][16][KVL] fp32 (heads >= H zero)
   float* part;      // [B][nsplit][16][KVL + 2]: acc, then max and sum
+  float* mix;       // [B][16][KVL] fp32: merged, rounded to the buffer dtype
   int nsplit, tiles_per_cta;
   bool w_vec;       // kv_b_proj.weight rows are 16-byte-aligned unit-stride ranges
 };
@@ -125,21 +127,22 @@ __device__ __forceinline__ void ld8(const MlaParams& p, const T* w, int64_t row,
 }
 
 // ---------------------------------------------------------------------------
-// One CTA per (head, 128-channel slab): reads its slab of W_nope once for all
-// batch rows.  Thread t: 8-channel chunk t % 16 of the slab, rows d = t / 16,
-// t / 16 + 16, ...; the 16 row-partials meet in shared memory.
-constexpr int QL_COLS = 128;      // channels per CTA
+// One CTA per (head, 64-channel slab): reads its slab of W_nope once for all
+// batch rows.  Thread t: 8-channel chunk t % 8 of the slab, rows d = t / 8,
+// t / 8 + 32, ...; the 32 row-partials meet in shared memory.
+constexpr int QL_COLS = 64;       // channels per CTA
+constexpr int QL_RG = 32;         // row groups per CTA
 constexpr int QL_BB = 4;          // batch rows per pass
 
 template <typename T>
 __global__ void __launch_bounds__(256)
 mla_qlat_kernel(const MlaParams p) {
-  extern __shared__ float sh[];   // q_nope of QL_BB rows [QL_BB][DN], partials [16][QL_BB][128]
+  extern __shared__ float sh[];   // q_nope of QL_BB rows [QL_BB][DN], partials [32][QL_BB][64]
   float* qs = sh;
   float* part = sh + QL_BB * ((p.DN + 3) & ~3);
   const int DNP = (p.DN + 3) & ~3;
   const int h = blockIdx.x, c0 = blockIdx.y * QL_COLS, tid = threadIdx.x;
-  const int chunk = tid & 15, dsub = tid >> 4;
+  const int chunk = tid & 7, dsub = tid >> 3;
   if (h == 0 && blockIdx.y == 0) {                    // kv_buf[b, pos] = c_kv[b]
     const int64_t pos = *p.pos;
     if (pos >= 0 && pos < p.L) {
@@ -175,15 +178,15 @@ mla_qlat_kernel(const MlaParams p) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[bb][e] = 0.f;
     if (8 * chunk < ncols) {
-      // rows d = dsub + 16 k, four at a time: their weight loads overlap
-      for (int d0 = dsub; d0 < p.DN; d0 += 64) {
+      // rows d = dsub + 32 k, four at a time: their weight loads overlap
+      for (int d0 = dsub; d0 < p.DN; d0 += 4 * QL_RG) {
         float x[4][8];
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          if (d0 + 16 * u < p.DN) ld8(p, wb, d0 + 16 * u, c0 + 8 * chunk, x[u]);
+          if (d0 + QL_RG * u < p.DN) ld8(p, wb, d0 + QL_RG * u, c0 + 8 * chunk, x[u]);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int d = d0 + 16 * u;
+          const int d = d0 + QL_RG * u;
           if (d >= p.DN) break;
 #pragma unroll
           for (int bb = 0; bb < QL_BB; ++bb) {
@@ -205,7 +208,7 @@ mla_qlat_kernel(const MlaParams p) {
       if (c >= ncols) continue;
       float x = 0.f;
 #pragma unroll
-      for (int ds = 0; ds < 16; ++ds) x += part[(ds * QL_BB + bb) * QL_COLS + c];
+      for (int ds = 0; ds < QL_RG; ++ds) x += part[(ds * QL_BB + bb) * QL_COLS + c];
       p.qlat[((size_t)(b0 + bb) * HM + h) * p.KVL + c0 + c] = x;
     }
   }
@@ -219,7 +222,9 @@ struct AttnCfg {
   static constexpr int KW = KVL / NW;                 // score channels per warp
   static constexpr int KSTEPS = KW / 16;
   static constexpr int NTW = KVL / NW / 8;            // mixing n-tiles per warp
-  static constexpr int OFF_P = 2 * TILE;              // P [16][64] in T, pitch PP
+  // tile stages in flight: three where they fit
+  static constexpr int NST = 3 * TILE + HM * PP + NW * HM * TS * 4 + 128 <= 227 * 1024 ? 3 : 2;
+  static constexpr int OFF_P = NST * TILE;            // P [16][64] in T, pitch PP
   static constexpr int OFF_RED = OFF_P + HM * PP;     // [NW][16][64] fp32 score partials
   static constexpr int OFF_ALPHA = OFF_RED + NW * HM * TS * 4;   // [16] rescale factors
   static constexpr int OFF_BAR = OFF_ALPHA + HM * 4;
@@ -235,8 +240,9 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
   uint8_t* Ps = sm + C::OFF_P;
   float* red = reinterpret_cast<float*>(sm + C::OFF_RED);
   float* alpha_s = reinterpret_cast<float*>(sm + C::OFF_ALPHA);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);   // [2]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
+  constexpr int NST = C::NST;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);   // [NST]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + NST);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
@@ -250,8 +256,7 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
   const int lm_hi = lane >> 4;
 
   if (tid == 0) {
-    ptx::mbar_init(&full[0], 1);
-    ptx::mbar_init(&full[1], 1);
+    for (int st = 0; st < NST; ++st) ptx::mbar_init(&full[st], 1);
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
@@ -263,7 +268,7 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
   };
   uint32_t pending = 0, pend_par = 0;
   if (tid == 0) {
-    for (int i = 0; i < 2 && t_beg + i < t_end; ++i) {
+    for (int i = 0; i < NST && t_beg + i < t_end; ++i) {
       fetch(t_beg + i, i);
       pending |= 1u << i;
     }
@@ -297,9 +302,9 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
 
   int k = 0;
   for (int t = t_beg; t < t_end; ++t, ++k) {
-    const int stage = k & 1;
+    const int stage = k % NST;
     const uint8_t* tile = sm + stage * C::TILE;
-    if (ptx::mbar_wait(&full[stage], (k >> 1) & 1, kWaitNs)) {
+    if (ptx::mbar_wait(&full[stage], (k / NST) & 1, kWaitNs)) {
       if (tid == 0) pending &= ~(1u << stage);
     } else {
       *abort_flag = 1;
@@ -401,18 +406,18 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
       }
     }
     __syncthreads();                                  // stage, P and red free
-    if (tid == 0 && t + 2 < t_end) {
+    if (tid == 0 && t + NST < t_end) {
       ptx::fence_proxy_async_smem();
-      fetch(t + 2, stage);
+      fetch(t + NST, stage);
       pending |= 1u << stage;
-      pend_par = (pend_par & ~(1u << stage)) | ((((k + 2) >> 1) & 1u) << stage);
+      pend_par = (pend_par & ~(1u << stage)) | ((((k + NST) / NST) & 1u) << stage);
     }
   }
 
   if (*abort_flag) {
     if (tid == 0) {
       atomicExch(&g_mla_device_error, 5);
-      for (int st = 0; st < 2; ++st)
+      for (int st = 0; st < NST; ++st)
         if (pending & (1u << st)) ptx::mbar_wait(&full[st], (pend_par >> st) & 1u, kWaitNs / 2);
     }
     return;
@@ -433,34 +438,43 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
 }
 
 // ---------------------------------------------------------------------------
+// mla_mix_kernel: one CTA per (128-channel slab, head, batch row), a thread per
+// channel: merges the splits' partials into mixed = sum p kv_buf / sum p,
+// rounded to the buffer dtype (the reference's p.to(buf.dtype) @ buf returns
+// that dtype), kept as fp32 in the workspace.
+constexpr int MX_COLS = 128;
+
 template <typename T>
-__global__ void __launch_bounds__(256)
-mla_combine_kernel(const MlaParams p) {
-  extern __shared__ float mixed[];                    // [KVL] fp32 (rounded to T)
+__global__ void __launch_bounds__(MX_COLS)
+mla_mix_kernel(const MlaParams p) {
   __shared__ float wsc[kMaxSplits];
-  __shared__ float tot;
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  const int lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[MX_COLS / 32];
+  __shared__ float max_s, tot_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x * MX_COLS + tid, h = blockIdx.y, b = blockIdx.z;
   const int KVL = p.KVL, ns = p.nsplit;
   const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
   const size_t sstride = (size_t)HM * (KVL + 2);
-  // split weights exp(m_i - M) and the total sum, all threads in parallel
-  __shared__ float red[8];
-  float mi = -INFINITY, li = 0.f;
-  if (tid < ns) {
-    mi = pb[tid * sstride + KVL];
-    li = pb[tid * sstride + KVL + 1];
-  }
-  float M = mi;
+  float M = -INFINITY;
+  for (int i = tid; i < ns; i += MX_COLS) M = fmaxf(M, pb[i * sstride + KVL]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   if (lane == 0) red[warp] = M;
   __syncthreads();
-  M = red[0];
-  for (int w = 1; w < (int)(blockDim.x / 32); ++w) M = fmaxf(M, red[w]);
-  const float wi = (tid < ns && mi != -INFINITY) ? expf(mi - M) : 0.f;
-  if (tid < ns) wsc[tid] = wi;
-  float lw = wi * li;
+  if (tid == 0) {
+    float m = red[0];
+    for (int w = 1; w < MX_COLS / 32; ++w) m = fmaxf(m, red[w]);
+    max_s = m;
+  }
+  __syncthreads();
+  M = max_s;
+  float lw = 0.f;
+  for (int i = tid; i < ns; i += MX_COLS) {
+    const float mi = pb[i * sstride + KVL];
+    const float wi = mi == -INFINITY ? 0.f : expf(mi - M);
+    wsc[i] = wi;
+    lw = fmaf(wi, pb[i * sstride + KVL + 1], lw);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
   __syncthreads();                                    // every thread has read red[] (max)
@@ -468,52 +482,82 @@ mla_combine_kernel(const MlaParams p) {
   __syncthreads();
   if (tid == 0) {
     float t = 0.f;
-    for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += red[w];
-    tot = t;
+    for (int w = 0; w < MX_COLS / 32; ++w) t += red[w];
+    tot_s = t;
   }
   __syncthreads();
-  const float inv = tot > 0.f ? 1.f / tot : 0.f;
-  for (int c = tid; c < KVL; c += blockDim.x) {
-    // eight independent partial sums: the split loads overlap instead of
-    // waiting one after another
-    float xs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int i = 0;
-    for (; i + 8 <= ns; i += 8) {
-      float v[8];
+  if (c >= KVL) return;
+  const float inv = tot_s > 0.f ? 1.f / tot_s : 0.f;
+  // sixteen independent partial sums: the split loads overlap
+  float xs[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = pb[(size_t)(i + u) * sstride + c];
+  for (int u = 0; u < 16; ++u) xs[u] = 0.f;
+  for (int i = 0; i < ns; i += 16) {
+    float v[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) xs[u] = fmaf(wsc[i + u], v[u], xs[u]);
-    }
-    for (; i < ns; ++i) xs[0] = fmaf(wsc[i], pb[(size_t)i * sstride + c], xs[0]);
-    const float x = ((xs[0] + xs[1]) + (xs[2] + xs[3])) + ((xs[4] + xs[5]) + (xs[6] + xs[7]));
-    const T r = static_cast<T>(x * inv);              // mixed in the buffer dtype
-    mixed[c] = static_cast<float>(r);
+    for (int u = 0; u < 16; ++u) v[u] = i + u < ns ? pb[(size_t)(i + u) * sstride + c] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) xs[u] = fmaf(i + u < ns ? wsc[i + u] : 0.f, v[u], xs[u]);
   }
-  __syncthreads();
-  // out[b, h, d] = mixed . W_v[h, d]: warp w takes rows d = w, w + 8, ...;
-  // lanes 8-channel chunks (16-byte loads), then a warp sum
+  float x = 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; ++u) x += xs[u];
+  p.mix[((size_t)b * HM + h) * KVL + c] = static_cast<float>(static_cast<T>(x * inv));
+}
+
+// mla_out_kernel: one CTA per (head, 16 rows of W_v): out[b, h, d] =
+// mixed[b, h] . W_v[h, d] in fp32 for every batch row; each W_v row is read
+// once.  Warp w owns rows 2w and 2w + 1 of the block (kept in registers),
+// lanes 8-channel chunks, a warp sum per (row, batch row).  Advances pos.
+constexpr int OUT_ROWS = 16;
+constexpr int OUT_BB = 8;         // batch rows of mixed staged per pass
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+mla_out_kernel(const MlaParams p) {
+  extern __shared__ float mx[];   // [OUT_BB][KVL]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.x, KVL = p.KVL, nch = KVL / 8;
   const T* wv = static_cast<const T*>(p.w) + ((int64_t)h * (p.DN + p.DV) + p.DN) * p.w_s[0];
-  T* ob = static_cast<T*>(p.out) + b * p.o_s[0] + h * p.o_s[1];
-  const int nch = KVL / 8;
-  for (int d = warp; d < p.DV; d += blockDim.x / 32) {
-    float s = 0.f;
+  float x[2][2][8];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int ch = lane + 32 * j;
-      if (ch < nch) {
-        float x[8];
-        ld8(p, wv, d, 8 * ch, x);
+      const int d = blockIdx.y * OUT_ROWS + 2 * warp + r, ch = lane + 32 * j;
+      if (d < p.DV && ch < nch) ld8(p, wv, d, 8 * ch, x[r][j]);
+    }
+  for (int b0 = 0; b0 < p.B; b0 += OUT_BB) {
+    const int nb = min(OUT_BB, p.B - b0);
+    __syncthreads();                                  // mx free
+    for (int i = tid; i < nb * KVL; i += blockDim.x) {
+      const int bb = i / KVL, c = i - bb * KVL;
+      mx[bb * KVL + c] = p.mix[((size_t)(b0 + bb) * HM + h) * KVL + c];
+    }
+    __syncthreads();
+    for (int bb = 0; bb < nb; ++bb) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s = fmaf(mixed[8 * ch + e], x[e], s);
+      for (int r = 0; r < 2; ++r) {
+        const int d = blockIdx.y * OUT_ROWS + 2 * warp + r;
+        float sacc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int ch = lane + 32 * j;
+          if (d < p.DV && ch < nch)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sacc = fmaf(mx[bb * KVL + 8 * ch + e], x[r][j][e], sacc);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, off);
+        if (lane == 0 && d < p.DV) {
+          T* ob = static_cast<T*>(p.out) + (b0 + bb) * p.o_s[0] + h * p.o_s[1];
+          st(ob + (int64_t)d * p.o_s[2], sacc);
+        }
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) st(ob + (int64_t)d * p.o_s[2], s);
   }
-  if (h == 0 && b == 0 && tid == 0) {
-    // every CTA has read what it needs of pos (the attention kernel is done)
+  if (h == 0 && blockIdx.y == 0 && tid == 0) {
+    // the attention kernel, the last reader of pos, has finished
     *p.pos += 1;
   }
 }
@@ -554,7 +598,8 @@ size_t ws_bytes(int B, int L, int KVL) {
   plan(B, L, device_sms(), &ns, &tpc);
   const size_t qlat = (size_t)B * HM * KVL * 4;
   const size_t part = (size_t)B * ns * HM * (KVL + 2) * 4;
-  return ((qlat + 255) / 256) * 256 + part;
+  const size_t mix = (size_t)B * HM * KVL * 4;
+  return ((qlat + 255) / 256) * 256 + ((part + 255) / 256) * 256 + mix;
 }
 
 bool kvl_ok(int kvl) { return kvl == 64 || kvl == 128 || kvl == 256 || kvl == 512; }
@@ -592,7 +637,7 @@ cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t 
 
 template <typename T>
 cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
-  const size_t qsm = (size_t)(QL_BB * ((p.DN + 3) & ~3) + 16 * QL_BB * QL_COLS) * sizeof(float);
+  const size_t qsm = (size_t)(QL_BB * ((p.DN + 3) & ~3) + QL_RG * QL_BB * QL_COLS) * sizeof(float);
   if (qsm > 48 * 1024) {
     cudaError_t ea = cudaFuncSetAttribute(mla_qlat_kernel<T>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
@@ -608,7 +653,11 @@ cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s
     default: e = launch_attn<T, 512>(p, tm, s); break;
   }
   if (e != cudaSuccess) return e;
-  mla_combine_kernel<T><<<dim3(p.H, p.B), 256, p.KVL * sizeof(float), s>>>(p);
+  mla_mix_kernel<T><<<dim3((p.KVL + MX_COLS - 1) / MX_COLS, p.H, p.B), MX_COLS, 0, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t osm = (size_t)OUT_BB * p.KVL * sizeof(float);
+  mla_out_kernel<T><<<dim3(p.H, (p.DV + OUT_ROWS - 1) / OUT_ROWS), 256, osm, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -662,6 +711,8 @@ int mla_decode_fwd(const MlaDecodeArgs* a, void* stream) {
   const size_t qlat = (size_t)p.B * HM * p.KVL * 4;
   p.qlat = reinterpret_cast<float*>(ws);
   p.part = reinterpret_cast<float*>(ws + ((qlat + 255) / 256) * 256);
+  const size_t part_b = (size_t)p.B * p.nsplit * HM * (p.KVL + 2) * 4;
+  p.mix = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.part) + ((part_b + 255) / 256) * 256);
   // kv_buf [B, L, KVL] as a 3-D tensor map: boxes of 64 channels x 64 positions
   EncodeTiled enc = encode_tiled();
   if (enc == nullptr) return KDA_ERR_LAUNCH;

@@ -198,10 +198,11 @@ mla_qlat_kernel(const MlaParams p) {
       }
     }
 #pragma unroll
-    for (int bb = 0; bb < QL_BB; ++bb)
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        part[(dsub * QL_BB + bb) * QL_COLS + 8 * chunk + e] = acc[bb][e];
+    for (int bb = 0; bb < QL_BB; ++bb) {
+      float4* dst = reinterpret_cast<float4*>(part + (dsub * QL_BB + bb) * QL_COLS + 8 * chunk);
+      dst[0] = make_float4(acc[bb][0], acc[bb][1], acc[bb][2], acc[bb][3]);
+      dst[1] = make_float4(acc[bb][4], acc[bb][5], acc[bb][6], acc[bb][7]);
+    }
     __syncthreads();
     for (int i = tid; i < nb * QL_COLS; i += blockDim.x) {
       const int bb = i / QL_COLS, c = i - bb * QL_COLS;
@@ -525,7 +526,12 @@ mla_out_kernel(const MlaParams p) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int d = blockIdx.y * OUT_ROWS + 2 * warp + r, ch = lane + 32 * j;
-      if (d < p.DV && ch < nch) ld8(p, wv, d, 8 * ch, x[r][j]);
+      if (d < p.DV && ch < nch) {
+        ld8(p, wv, d, 8 * ch, x[r][j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[r][j][e] = 0.f;
+      }
     }
   for (int b0 = 0; b0 < p.B; b0 += OUT_BB) {
     const int nb = min(OUT_BB, p.B - b0);
@@ -536,22 +542,38 @@ mla_out_kernel(const MlaParams p) {
     }
     __syncthreads();
     for (int bb = 0; bb < nb; ++bb) {
+      // this lane's chunks of mixed[bb] (two 16-byte loads each), for both rows
+      float m[2][8];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int d = blockIdx.y * OUT_ROWS + 2 * warp + r;
-        float sacc = 0.f;
+      for (int j = 0; j < 2; ++j) {
+        const int ch = lane + 32 * j;
+        if (ch < nch) {
+          const float4 a = *reinterpret_cast<const float4*>(mx + bb * KVL + 8 * ch);
+          const float4 c = *reinterpret_cast<const float4*>(mx + bb * KVL + 8 * ch + 4);
+          m[j][0] = a.x; m[j][1] = a.y; m[j][2] = a.z; m[j][3] = a.w;
+          m[j][4] = c.x; m[j][5] = c.y; m[j][6] = c.z; m[j][7] = c.w;
+        }
+      }
+      float sacc[2] = {0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int ch = lane + 32 * j;
-          if (d < p.DV && ch < nch)
+          if (ch < nch)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sacc = fmaf(mx[bb * KVL + 8 * ch + e], x[r][j][e], sacc);
+            for (int e = 0; e < 8; ++e) sacc[r] = fmaf(m[j][e], x[r][j][e], sacc[r]);
         }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, off);
-        if (lane == 0 && d < p.DV) {
+      for (int off = 16; off > 0; off >>= 1) {
+        sacc[0] += __shfl_xor_sync(0xffffffffu, sacc[0], off);
+        sacc[1] += __shfl_xor_sync(0xffffffffu, sacc[1], off);
+      }
+      if (lane < 2) {
+        const int d = blockIdx.y * OUT_ROWS + 2 * warp + lane;
+        if (d < p.DV) {
           T* ob = static_cast<T*>(p.out) + (b0 + bb) * p.o_s[0] + h * p.o_s[1];
-          st(ob + (int64_t)d * p.o_s[2], sacc);
+          st(ob + (int64_t)d * p.o_s[2], lane ? sacc[1] : sacc[0]);
         }
       }
     }

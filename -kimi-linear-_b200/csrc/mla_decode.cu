@@ -11,9 +11,11 @@
 //   out[b, h]      = mixed[b, h] W_v[h]^T                         (fp32, then I/O dtype)
 //   pos           += 1
 // Four kernels on the caller's stream, reading `pos` from device memory
-// (graph-capturable):
-//  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, b)); CTA (0, b) also
-//    writes the new latent row at pos;
+// (graph-capturable).  The last three are launched as programmatic dependents
+// of the one before (launch, barrier set-up, the tile loads that do not need
+// the previous kernel's output and the W_v loads overlap its tail):
+//  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, 64-channel slab)); the
+//    CTAs of head h also write batch row h's new latent row at pos;
 //  * mla_attn_kernel: flash decoding.  One CTA per (split, b) walks 64-position
 //    tiles of kv_buf[b] (tiles past pos are not loaded), three TMA stages with a
 //    128-byte swizzle.  Scores: f16/bf16 mma.sync with q_lat split into hi + lo
@@ -27,6 +29,7 @@
 #include <cuda.h>
 #include <cstring>
 #include <type_traits>
+#include <utility>
 
 #include "kda_internal.cuh"
 #include "tc_ptx.cuh"
@@ -129,7 +132,10 @@ __device__ __forceinline__ void ld8(const MlaParams& p, const T* w, int64_t row,
 // ---------------------------------------------------------------------------
 // One CTA per (head, 64-channel slab): reads its slab of W_nope once for all
 // batch rows.  Thread t: 8-channel chunk t % 8 of the slab, rows d = t / 8,
-// t / 8 + 32, ...; the 32 row-partials meet in shared memory.
+// t / 8 + 32, ...; the 32 row-partials meet in shared memory.  All loads of a
+// pass (weights, q_nope, the new latent row) are issued before their first use.
+// CTA (h, y) also copies c_kv[b] into kv_buf[b, pos] for b = h, h + 16, ...
+// over its channel slab.
 constexpr int QL_COLS = 64;       // channels per CTA
 constexpr int QL_RG = 32;         // row groups per CTA
 constexpr int QL_BB = 4;          // batch rows per pass
@@ -137,66 +143,71 @@ constexpr int QL_BB = 4;          // batch rows per pass
 template <typename T>
 __global__ void __launch_bounds__(256)
 mla_qlat_kernel(const MlaParams p) {
-  extern __shared__ float sh[];   // q_nope of QL_BB rows [QL_BB][DN], partials [32][QL_BB][64]
-  float* qs = sh;
-  float* part = sh + QL_BB * ((p.DN + 3) & ~3);
-  const int DNP = (p.DN + 3) & ~3;
+  extern __shared__ float part[];  // [QL_RG][QL_BB][QL_COLS] row partials
   const int h = blockIdx.x, c0 = blockIdx.y * QL_COLS, tid = threadIdx.x;
   const int chunk = tid & 7, dsub = tid >> 3;
-  if (h == 0 && blockIdx.y == 0) {                    // kv_buf[b, pos] = c_kv[b]
-    const int64_t pos = *p.pos;
-    if (pos >= 0 && pos < p.L) {
-      for (int b = 0; b < p.B; ++b) {
-        const T* src = static_cast<const T*>(p.c_kv) + b * p.c_s[0];
-        T* dst = static_cast<T*>(p.kv_buf) + b * p.kv_s[0] + pos * p.kv_s[1];
-        for (int c = tid; c < p.KVL; c += blockDim.x) dst[c] = src[(int64_t)c * p.c_s[1]];
-      }
-    } else if (tid == 0) {
-      atomicExch(&g_mla_device_error, 4);             // position outside the buffer
-    }
-  }
   const int ncols = min(QL_COLS, p.KVL - c0);         // KVL = 64: half a slab
+  ptx::grid_dep_launch();                             // the attention grid may start launching
+  // kv_buf[b, pos] = c_kv[b]: loads here, stores after the weight loads
+  const int64_t pos = *p.pos;
+  const bool pos_ok = pos >= 0 && pos < p.L;
+  const bool lat = tid < ncols && h < p.B;
+  T lat_v{};
+  if (lat) lat_v = static_cast<const T*>(p.c_kv)[h * p.c_s[0] + (int64_t)(c0 + tid) * p.c_s[1]];
+  auto write_latent = [&]() {
+    if (!pos_ok) {
+      if (h == 0 && blockIdx.y == 0 && tid == 0)
+        atomicExch(&g_mla_device_error, 4);           // position outside the buffer
+      return;
+    }
+    T* row = static_cast<T*>(p.kv_buf) + pos * p.kv_s[1] + c0;   // unit channel stride
+    if (lat) row[h * p.kv_s[0] + tid] = lat_v;
+    for (int b = h + HM; b < p.B; b += HM)            // more than 16 batch rows
+      for (int c = tid; c < ncols; c += blockDim.x)
+        row[b * p.kv_s[0] + c] =
+            static_cast<const T*>(p.c_kv)[b * p.c_s[0] + (int64_t)(c0 + c) * p.c_s[1]];
+  };
   if (h >= p.H) {                                     // padded head rows: zero
     for (int b = 0; b < p.B; ++b)
       for (int c = tid; c < ncols; c += blockDim.x)
         p.qlat[((size_t)b * HM + h) * p.KVL + c0 + c] = 0.f;
+    write_latent();
     return;
   }
   const T* wb = static_cast<const T*>(p.w) + (int64_t)h * (p.DN + p.DV) * p.w_s[0];
+  const T* qn = static_cast<const T*>(p.q_nope) + h * p.q_s[1];
   for (int b0 = 0; b0 < p.B; b0 += QL_BB) {
     const int nb = min(QL_BB, p.B - b0);
-    __syncthreads();                                  // qs / part free
-    for (int i = tid; i < nb * p.DN; i += blockDim.x) {
-      const int bb = i / p.DN, d = i - bb * p.DN;
-      const T* qn = static_cast<const T*>(p.q_nope) + (b0 + bb) * p.q_s[0] + h * p.q_s[1];
-      qs[bb * DNP + d] = ld(qn + (int64_t)d * p.q_s[2]);
-    }
-    __syncthreads();
     float acc[QL_BB][8];
 #pragma unroll
     for (int bb = 0; bb < QL_BB; ++bb)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[bb][e] = 0.f;
     if (8 * chunk < ncols) {
-      // rows d = dsub + 32 k, four at a time: their weight loads overlap
+      // rows d = dsub + 32 k, four at a time: their weight and q_nope loads overlap
       for (int d0 = dsub; d0 < p.DN; d0 += 4 * QL_RG) {
-        float x[4][8];
+        float x[4][8], qv[4][QL_BB];
 #pragma unroll
         for (int u = 0; u < 4; ++u)
           if (d0 + QL_RG * u < p.DN) ld8(p, wb, d0 + QL_RG * u, c0 + 8 * chunk, x[u]);
 #pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int bb = 0; bb < QL_BB; ++bb)
+            qv[u][bb] = (d0 + QL_RG * u < p.DN && bb < nb)
+                            ? ld(qn + (b0 + bb) * p.q_s[0] + (int64_t)(d0 + QL_RG * u) * p.q_s[2])
+                            : 0.f;
+#pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int d = d0 + QL_RG * u;
-          if (d >= p.DN) break;
+          if (d0 + QL_RG * u >= p.DN) break;
 #pragma unroll
-          for (int bb = 0; bb < QL_BB; ++bb) {
-            const float qd = bb < nb ? qs[bb * DNP + d] : 0.f;
+          for (int bb = 0; bb < QL_BB; ++bb)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[bb][e] = fmaf(qd, x[u][e], acc[bb][e]);
-          }
+            for (int e = 0; e < 8; ++e) acc[bb][e] = fmaf(qv[u][bb], x[u][e], acc[bb][e]);
         }
       }
     }
+    __syncthreads();                                  // part free
 #pragma unroll
     for (int bb = 0; bb < QL_BB; ++bb) {
       float4* dst = reinterpret_cast<float4*>(part + (dsub * QL_BB + bb) * QL_COLS + 8 * chunk);
@@ -213,6 +224,7 @@ mla_qlat_kernel(const MlaParams p) {
       p.qlat[((size_t)(b0 + bb) * HM + h) * p.KVL + c0 + c] = x;
     }
   }
+  write_latent();
 }
 
 // ---------------------------------------------------------------------------
@@ -261,16 +273,30 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
+  ptx::grid_dep_launch();                             // the mix grid may start launching
   __syncthreads();
   auto fetch = [&](int t, int stage) {                // thread 0 only
     ptx::mbar_arrive_expect_tx(&full[stage], C::TILE);
     for (int g = 0; g < C::GROUPS; ++g)
       ptx::tma_load_3d(sm + stage * C::TILE + g * TS * 128, &tm, 64 * g, t * TS, b, &full[stage]);
   };
+  // Only the tile holding pos is written by the q_lat grid (the new latent
+  // row): the other first-stage tiles load while that grid is still running.
   uint32_t pending = 0, pend_par = 0;
+  const int pos_tile = last / TS;
   if (tid == 0) {
     for (int i = 0; i < NST && t_beg + i < t_end; ++i) {
+      if (t_beg + i == pos_tile) continue;
       fetch(t_beg + i, i);
+      pending |= 1u << i;
+    }
+  }
+  ptx::grid_dep_wait();                               // q_lat and kv_buf[., pos] visible
+  if (tid == 0) {
+    const int i = pos_tile - t_beg;
+    if (i >= 0 && i < NST && pos_tile < t_end) {
+      ptx::fence_proxy_async_global();
+      fetch(pos_tile, i);
       pending |= 1u << i;
     }
   }
@@ -454,6 +480,8 @@ mla_mix_kernel(const MlaParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = blockIdx.x * MX_COLS + tid, h = blockIdx.y, b = blockIdx.z;
   const int KVL = p.KVL, ns = p.nsplit;
+  ptx::grid_dep_wait();                               // the attention partials are visible
+  ptx::grid_dep_launch();                             // the output grid may start launching
   const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
   const size_t sstride = (size_t)HM * (KVL + 2);
   float M = -INFINITY;
@@ -533,6 +561,7 @@ mla_out_kernel(const MlaParams p) {
         for (int e = 0; e < 8; ++e) x[r][j][e] = 0.f;
       }
     }
+  ptx::grid_dep_wait();                               // mixed is visible
   for (int b0 = 0; b0 < p.B; b0 += OUT_BB) {
     const int nb = min(OUT_BB, p.B - b0);
     __syncthreads();                                  // mx free
@@ -647,24 +676,39 @@ int validate(const MlaDecodeArgs* a) {
   return KDA_OK;
 }
 
+// launch with programmatic stream serialization: the grid may start while the
+// previous kernel on the stream is still running (after all of that kernel's
+// CTAs have called griddepcontrol.launch_dependents); it calls
+// griddepcontrol.wait before touching anything that kernel writes
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*k)(Params...), dim3 grid, int threads, size_t smem,
+                             cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 template <typename T, int KVL>
 cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
   auto k = mla_attn_kernel<T, KVL>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        AttnCfg<T, KVL>::SMEM);
   if (e != cudaSuccess) return e;
-  k<<<dim3(p.nsplit, p.B), NW * 32, AttnCfg<T, KVL>::SMEM, s>>>(p, tm);
-  return cudaGetLastError();
+  return launch_dependent(k, dim3(p.nsplit, p.B), NW * 32, AttnCfg<T, KVL>::SMEM, s, p, tm);
 }
 
 template <typename T>
 cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
-  const size_t qsm = (size_t)(QL_BB * ((p.DN + 3) & ~3) + QL_RG * QL_BB * QL_COLS) * sizeof(float);
-  if (qsm > 48 * 1024) {
-    cudaError_t ea = cudaFuncSetAttribute(mla_qlat_kernel<T>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
-    if (ea != cudaSuccess) return ea;
-  }
+  // the first kernel follows foreign work on the stream: an ordinary launch
+  const size_t qsm = (size_t)QL_RG * QL_BB * QL_COLS * sizeof(float);
   mla_qlat_kernel<T><<<dim3(HM, (p.KVL + QL_COLS - 1) / QL_COLS), 256, qsm, s>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -675,12 +719,12 @@ cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s
     default: e = launch_attn<T, 512>(p, tm, s); break;
   }
   if (e != cudaSuccess) return e;
-  mla_mix_kernel<T><<<dim3((p.KVL + MX_COLS - 1) / MX_COLS, p.H, p.B), MX_COLS, 0, s>>>(p);
-  e = cudaGetLastError();
+  e = launch_dependent(mla_mix_kernel<T>, dim3((p.KVL + MX_COLS - 1) / MX_COLS, p.H, p.B),
+                       MX_COLS, 0, s, p);
   if (e != cudaSuccess) return e;
   const size_t osm = (size_t)OUT_BB * p.KVL * sizeof(float);
-  mla_out_kernel<T><<<dim3(p.H, (p.DV + OUT_ROWS - 1) / OUT_ROWS), 256, osm, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(mla_out_kernel<T>, dim3(p.H, (p.DV + OUT_ROWS - 1) / OUT_ROWS), 256,
+                          osm, s, p);
 }
 
 }  // namespace

@@ -139,6 +139,20 @@ __device__ __forceinline__ uint32_t num_sms() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// order this thread's view of global memory before its later async-proxy (TMA) reads
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// programmatic dependent launch: wait until the preceding grid has completed
+// and its writes are visible / let the next grid start launching.  Both are
+// no-ops for a kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05

@@ -10,8 +10,8 @@
 //   mixed[b, h]    = sum_s p kv_buf[b, s]      (p and the result in kv_buf's dtype)
 //   out[b, h]      = mixed[b, h] W_v[h]^T                         (fp32, then I/O dtype)
 //   pos           += 1
-// Four kernels on the caller's stream, reading `pos` from device memory
-// (graph-capturable).  The last three are launched as programmatic dependents
+// Three kernels on the caller's stream, reading `pos` from device memory
+// (graph-capturable).  The last two are launched as programmatic dependents
 // of the one before (launch, barrier set-up, the tile loads that do not need
 // the previous kernel's output and the W_v loads overlap its tail):
 //  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, 64-channel slab)); the
@@ -22,10 +22,10 @@
 //    parts (fp32-level scores against exact buffer values), K split over the
 //    four warps and summed in shared memory; online softmax in fp32; mixing
 //    P . tile with N split over the warps.  Writes (max, sum, acc) partials;
-//  * mla_mix_kernel: merges the partials per (channel slab, h, b) and rounds
-//    mixed to the buffer dtype as the reference does;
-//  * mla_out_kernel: projects with W_v in fp32 (each W_v row read once for all
-//    batch rows) and advances pos.
+//  * mla_mixout_kernel: per (128-channel slab, h, b) merges the partials,
+//    rounds mixed to the buffer dtype as the reference does and projects the
+//    slab with W_v in fp32; the last slab CTA of (b, h) writes out[b, h].
+//    Advances pos.
 #include <cuda.h>
 #include <cstring>
 #include <type_traits>
@@ -45,6 +45,8 @@ constexpr int TS = 64;            // positions per tile
 constexpr int NW = 4;             // warps per attention CTA
 constexpr int HM = 16;            // heads per CTA (MMA M); H <= 16
 constexpr int PP = TS * 2 + 16;   // pitch of P [16][64] in bytes (conflict-free ldmatrix)
+constexpr int RP = TS + 8;        // pitch of the score partials [16][64] in floats: the
+                                  // eight fragment rows of a warp's stores hit distinct banks
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int kMaxSplits = 256;   // splits of the position range per batch row
 
@@ -104,8 +106,9 @@ struct MlaParams {
   void* out; int64_t o_s[3];
   float* qlat;      // [B][16][KVL] fp32 (heads >= H zero)
   float* part;      // [B][nsplit][16][KVL + 2]: acc, then max and sum
-  float* mix;       // [B][16][KVL] fp32: merged, rounded to the buffer dtype
-  int nsplit, tiles_per_cta;
+  float* opart;     // [B][16][nslab][DV] fp32 slab partials of out
+  int* count;       // [B][16] slab partials written (zeroed by the q_lat kernel)
+  int nsplit, tiles_per_cta, nslab;
   bool w_vec;       // kv_b_proj.weight rows are 16-byte-aligned unit-stride ranges
 };
 
@@ -148,6 +151,8 @@ mla_qlat_kernel(const MlaParams p) {
   const int chunk = tid & 7, dsub = tid >> 3;
   const int ncols = min(QL_COLS, p.KVL - c0);         // KVL = 64: half a slab
   ptx::grid_dep_launch();                             // the attention grid may start launching
+  if (blockIdx.y == 0)                                // slab-partial counters of this call
+    for (int b = tid; b < p.B; b += blockDim.x) p.count[b * HM + h] = 0;
   // kv_buf[b, pos] = c_kv[b]: loads here, stores after the weight loads
   const int64_t pos = *p.pos;
   const bool pos_ok = pos >= 0 && pos < p.L;
@@ -236,10 +241,10 @@ struct AttnCfg {
   static constexpr int KSTEPS = KW / 16;
   static constexpr int NTW = KVL / NW / 8;            // mixing n-tiles per warp
   // tile stages in flight: three where they fit
-  static constexpr int NST = 3 * TILE + HM * PP + NW * HM * TS * 4 + 128 <= 227 * 1024 ? 3 : 2;
+  static constexpr int NST = 3 * TILE + HM * PP + NW * HM * RP * 4 + 128 <= 227 * 1024 ? 3 : 2;
   static constexpr int OFF_P = NST * TILE;            // P [16][64] in T, pitch PP
-  static constexpr int OFF_RED = OFF_P + HM * PP;     // [NW][16][64] fp32 score partials
-  static constexpr int OFF_ALPHA = OFF_RED + NW * HM * TS * 4;   // [16] rescale factors
+  static constexpr int OFF_RED = OFF_P + HM * PP;     // [NW][16][RP] fp32 score partials
+  static constexpr int OFF_ALPHA = OFF_RED + NW * HM * RP * 4;   // [16] rescale factors
   static constexpr int OFF_BAR = OFF_ALPHA + HM * 4;
   static constexpr int SMEM = OFF_BAR + 64;
   static_assert(SMEM <= 227 * 1024, "mla shared memory");
@@ -273,7 +278,7 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
-  ptx::grid_dep_launch();                             // the mix grid may start launching
+  ptx::grid_dep_launch();                             // the merge grid may start launching
   __syncthreads();
   auto fetch = [&](int t, int stage) {                // thread 0 only
     ptx::mbar_arrive_expect_tx(&full[stage], C::TILE);
@@ -360,30 +365,40 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
       }
     }
     {
-      float* rw = red + warp * HM * TS;
+      float* rw = red + warp * HM * RP;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int s = 8 * nt + 2 * tig;
-        *reinterpret_cast<float2*>(rw + gid * TS + s) = make_float2(sc[nt][0], sc[nt][1]);
-        *reinterpret_cast<float2*>(rw + (gid + 8) * TS + s) = make_float2(sc[nt][2], sc[nt][3]);
+        *reinterpret_cast<float2*>(rw + gid * RP + s) = make_float2(sc[nt][0], sc[nt][1]);
+        *reinterpret_cast<float2*>(rw + (gid + 8) * RP + s) = make_float2(sc[nt][2], sc[nt][3]);
       }
     }
     __syncthreads();
     if (*abort_flag) break;
-    // ---- online softmax: thread -> head hh, positions 8 q .. 8 q + 7
+    // ---- online softmax: thread -> head hh, positions 4 q .. 4 q + 3 and
+    // 32 + 4 q .. 32 + 4 q + 3 (16-byte reads: the eight threads of a head
+    // cover 128 contiguous bytes per read)
     {
       const int hh = tid >> 3, q = tid & 7;
       float v[8];
       float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int s = 8 * q + i;
-        float x = red[hh * TS + s] + red[HM * TS + hh * TS + s] + red[2 * HM * TS + hh * TS + s] +
-                  red[3 * HM * TS + hh * TS + s];
-        x *= p.scale;
-        if ((int64_t)t * TS + s > last || hh >= p.H) x = -INFINITY;
-        v[i] = x;
-        mt = fmaxf(mt, x);
+      for (int half = 0; half < 2; ++half) {
+        const int s0 = 32 * half + 4 * q;
+        float4 x = *reinterpret_cast<const float4*>(red + hh * RP + s0);
+#pragma unroll
+        for (int w = 1; w < NW; ++w) {
+          const float4 y = *reinterpret_cast<const float4*>(red + w * HM * RP + hh * RP + s0);
+          x.x += y.x; x.y += y.y; x.z += y.z; x.w += y.w;
+        }
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float xv = xs[i] * p.scale;
+          if ((int64_t)t * TS + s0 + i > last || hh >= p.H) xv = -INFINITY;
+          v[4 * half + i] = xv;
+          mt = fmaxf(mt, xv);
+        }
       }
 #pragma unroll
       for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
@@ -402,7 +417,8 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
       for (int off = 1; off < 8; off <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
       l_run = l_run * a + ls;
       m_run = m_new;
-      *reinterpret_cast<uint4*>(Ps + hh * PP + 16 * q) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint2*>(Ps + hh * PP + 8 * q) = make_uint2(pk[0], pk[1]);
+      *reinterpret_cast<uint2*>(Ps + hh * PP + 64 + 8 * q) = make_uint2(pk[2], pk[3]);
       if (q == 0) alpha_s[hh] = a;
     }
     __syncthreads();
@@ -465,27 +481,52 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
 }
 
 // ---------------------------------------------------------------------------
-// mla_mix_kernel: one CTA per (128-channel slab, head, batch row), a thread per
-// channel: merges the splits' partials into mixed = sum p kv_buf / sum p,
+// mla_mixout_kernel: one CTA per (128-channel slab, head, batch row), a thread
+// per channel: merges the splits' partials into mixed = sum p kv_buf / sum p,
 // rounded to the buffer dtype (the reference's p.to(buf.dtype) @ buf returns
-// that dtype), kept as fp32 in the workspace.
+// that dtype), then projects the slab with its columns of W_v (thread d: out
+// row d) in fp32 into a slab partial.  The last CTA of (b, h) to finish sums
+// the slab partials in slab order and writes out[b, h] in the I/O dtype.
+// CTA (0, 0, 0) advances pos.
 constexpr int MX_COLS = 128;
+constexpr int MX_PF = 48;         // splits loaded before the merge weights are known
 
 template <typename T>
 __global__ void __launch_bounds__(MX_COLS)
-mla_mix_kernel(const MlaParams p) {
+mla_mixout_kernel(const MlaParams p) {
   __shared__ float wsc[kMaxSplits];
   __shared__ float red[MX_COLS / 32];
+  __shared__ __align__(16) float mixed[MX_COLS];
   __shared__ float max_s, tot_s;
+  __shared__ int last_s;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x * MX_COLS + tid, h = blockIdx.y, b = blockIdx.z;
-  const int KVL = p.KVL, ns = p.nsplit;
+  const int slab = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int KVL = p.KVL, ns = p.nsplit, c0 = slab * MX_COLS, c = c0 + tid;
+  const int ncols = min(MX_COLS, KVL - c0);
+  // W_v[h, d = tid, slab]: no earlier grid of this call writes it, so its
+  // loads are issued before waiting for the attention grid
+  const T* wv = static_cast<const T*>(p.w) + ((int64_t)h * (p.DN + p.DV) + p.DN) * p.w_s[0];
+  const bool wpre = p.w_vec && tid < p.DV;
+  uint4 wr[MX_COLS / 8];
+#pragma unroll
+  for (int j = 0; j < MX_COLS / 8; ++j)
+    if (wpre && 8 * j < ncols)
+      wr[j] = *reinterpret_cast<const uint4*>(wv + (int64_t)tid * p.w_s[0] + c0 + 8 * j);
   ptx::grid_dep_wait();                               // the attention partials are visible
-  ptx::grid_dep_launch();                             // the output grid may start launching
+  if (slab == 0 && h == 0 && b == 0 && tid == 0) *p.pos += 1;   // its readers have finished
+
   const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
   const size_t sstride = (size_t)HM * (KVL + 2);
-  float M = -INFINITY;
-  for (int i = tid; i < ns; i += MX_COLS) M = fmaxf(M, pb[i * sstride + KVL]);
+  // this channel's values of the first MX_PF splits: in flight during the weights
+  float v[MX_PF];
+#pragma unroll
+  for (int u = 0; u < MX_PF; ++u) v[u] = (u < ns && tid < ncols) ? pb[u * sstride + c] : 0.f;
+  // (max, sum) of split tid (kMaxSplits <= 2 * MX_COLS: at most two per thread)
+  static_assert(kMaxSplits <= 2 * MX_COLS, "two splits per merge thread");
+  float2 ml0 = make_float2(-INFINITY, 0.f), ml1 = make_float2(-INFINITY, 0.f);
+  if (tid < ns) ml0 = *reinterpret_cast<const float2*>(pb + tid * sstride + KVL);
+  if (tid + MX_COLS < ns) ml1 = *reinterpret_cast<const float2*>(pb + (tid + MX_COLS) * sstride + KVL);
+  float M = fmaxf(ml0.x, ml1.x);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   if (lane == 0) red[warp] = M;
@@ -498,11 +539,15 @@ mla_mix_kernel(const MlaParams p) {
   __syncthreads();
   M = max_s;
   float lw = 0.f;
-  for (int i = tid; i < ns; i += MX_COLS) {
-    const float mi = pb[i * sstride + KVL];
-    const float wi = mi == -INFINITY ? 0.f : expf(mi - M);
-    wsc[i] = wi;
-    lw = fmaf(wi, pb[i * sstride + KVL + 1], lw);
+  if (tid < ns) {
+    const float wi = ml0.x == -INFINITY ? 0.f : expf(ml0.x - M);
+    wsc[tid] = wi;
+    lw = wi * ml0.y;
+  }
+  if (tid + MX_COLS < ns) {
+    const float wi = ml1.x == -INFINITY ? 0.f : expf(ml1.x - M);
+    wsc[tid + MX_COLS] = wi;
+    lw = fmaf(wi, ml1.y, lw);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
@@ -515,101 +560,66 @@ mla_mix_kernel(const MlaParams p) {
     tot_s = t;
   }
   __syncthreads();
-  if (c >= KVL) return;
   const float inv = tot_s > 0.f ? 1.f / tot_s : 0.f;
-  // sixteen independent partial sums: the split loads overlap
+  // sixteen independent partial sums (split i into sum i % 16)
   float xs[16];
 #pragma unroll
   for (int u = 0; u < 16; ++u) xs[u] = 0.f;
-  for (int i = 0; i < ns; i += 16) {
-    float v[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = i + u < ns ? pb[(size_t)(i + u) * sstride + c] : 0.f;
+  for (int u = 0; u < MX_PF; ++u) xs[u % 16] = fmaf(u < ns ? wsc[u] : 0.f, v[u], xs[u % 16]);
+  for (int i = MX_PF; i < ns; i += 16) {
+    float w16[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) xs[u] = fmaf(i + u < ns ? wsc[i + u] : 0.f, v[u], xs[u]);
+    for (int u = 0; u < 16; ++u) w16[u] = (i + u < ns && tid < ncols) ? pb[(i + u) * sstride + c] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) xs[u] = fmaf(i + u < ns ? wsc[i + u] : 0.f, w16[u], xs[u]);
   }
   float x = 0.f;
 #pragma unroll
   for (int u = 0; u < 16; ++u) x += xs[u];
-  p.mix[((size_t)b * HM + h) * KVL + c] = static_cast<float>(static_cast<T>(x * inv));
-}
+  if (tid < ncols) mixed[tid] = static_cast<float>(static_cast<T>(x * inv));
+  __syncthreads();
 
-// mla_out_kernel: one CTA per (head, 16 rows of W_v): out[b, h, d] =
-// mixed[b, h] . W_v[h, d] in fp32 for every batch row; each W_v row is read
-// once.  Warp w owns rows 2w and 2w + 1 of the block (kept in registers),
-// lanes 8-channel chunks, a warp sum per (row, batch row).  Advances pos.
-constexpr int OUT_ROWS = 16;
-constexpr int OUT_BB = 8;         // batch rows of mixed staged per pass
-
-template <typename T>
-__global__ void __launch_bounds__(256)
-mla_out_kernel(const MlaParams p) {
-  extern __shared__ float mx[];   // [OUT_BB][KVL]
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int h = blockIdx.x, KVL = p.KVL, nch = KVL / 8;
-  const T* wv = static_cast<const T*>(p.w) + ((int64_t)h * (p.DN + p.DV) + p.DN) * p.w_s[0];
-  float x[2][2][8];
+  // slab partial of out[b, h, d], d = tid, tid + 128, ...
+  float* op = p.opart + (((size_t)b * HM + h) * p.nslab + slab) * p.DV;
+  for (int d = tid; d < p.DV; d += MX_COLS) {
+    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};   // independent chains
 #pragma unroll
-  for (int r = 0; r < 2; ++r)
+    for (int j = 0; j < MX_COLS / 8; ++j) {
+      if (8 * j >= ncols) break;
+      float w8[8];
+      if (wpre && d == tid) {
+        const uint32_t u4[4] = {wr[j].x, wr[j].y, wr[j].z, wr[j].w};
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int d = blockIdx.y * OUT_ROWS + 2 * warp + r, ch = lane + 32 * j;
-      if (d < p.DV && ch < nch) {
-        ld8(p, wv, d, 8 * ch, x[r][j]);
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = MmaT<T>::unpack(u4[i]);
+          w8[2 * i] = f.x;
+          w8[2 * i + 1] = f.y;
+        }
       } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[r][j][e] = 0.f;
+        ld8(p, wv, d, c0 + 8 * j, w8);
       }
+      const float4 m0 = *reinterpret_cast<const float4*>(mixed + 8 * j);
+      const float4 m1 = *reinterpret_cast<const float4*>(mixed + 8 * j + 4);
+      acc8[0] = fmaf(m0.x, w8[0], acc8[0]); acc8[1] = fmaf(m0.y, w8[1], acc8[1]);
+      acc8[2] = fmaf(m0.z, w8[2], acc8[2]); acc8[3] = fmaf(m0.w, w8[3], acc8[3]);
+      acc8[4] = fmaf(m1.x, w8[4], acc8[4]); acc8[5] = fmaf(m1.y, w8[5], acc8[5]);
+      acc8[6] = fmaf(m1.z, w8[6], acc8[6]); acc8[7] = fmaf(m1.w, w8[7], acc8[7]);
     }
-  ptx::grid_dep_wait();                               // mixed is visible
-  for (int b0 = 0; b0 < p.B; b0 += OUT_BB) {
-    const int nb = min(OUT_BB, p.B - b0);
-    __syncthreads();                                  // mx free
-    for (int i = tid; i < nb * KVL; i += blockDim.x) {
-      const int bb = i / KVL, c = i - bb * KVL;
-      mx[bb * KVL + c] = p.mix[((size_t)(b0 + bb) * HM + h) * KVL + c];
-    }
-    __syncthreads();
-    for (int bb = 0; bb < nb; ++bb) {
-      // this lane's chunks of mixed[bb] (two 16-byte loads each), for both rows
-      float m[2][8];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int ch = lane + 32 * j;
-        if (ch < nch) {
-          const float4 a = *reinterpret_cast<const float4*>(mx + bb * KVL + 8 * ch);
-          const float4 c = *reinterpret_cast<const float4*>(mx + bb * KVL + 8 * ch + 4);
-          m[j][0] = a.x; m[j][1] = a.y; m[j][2] = a.z; m[j][3] = a.w;
-          m[j][4] = c.x; m[j][5] = c.y; m[j][6] = c.z; m[j][7] = c.w;
-        }
-      }
-      float sacc[2] = {0.f, 0.f};
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int ch = lane + 32 * j;
-          if (ch < nch)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sacc[r] = fmaf(m[j][e], x[r][j][e], sacc[r]);
-        }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        sacc[0] += __shfl_xor_sync(0xffffffffu, sacc[0], off);
-        sacc[1] += __shfl_xor_sync(0xffffffffu, sacc[1], off);
-      }
-      if (lane < 2) {
-        const int d = blockIdx.y * OUT_ROWS + 2 * warp + lane;
-        if (d < p.DV) {
-          T* ob = static_cast<T*>(p.out) + (b0 + bb) * p.o_s[0] + h * p.o_s[1];
-          st(ob + (int64_t)d * p.o_s[2], lane ? sacc[1] : sacc[0]);
-        }
-      }
-    }
+    op[d] = ((acc8[0] + acc8[1]) + (acc8[2] + acc8[3])) + ((acc8[4] + acc8[5]) + (acc8[6] + acc8[7]));
   }
-  if (h == 0 && blockIdx.y == 0 && tid == 0) {
-    // the attention kernel, the last reader of pos, has finished
-    *p.pos += 1;
+  // the barrier orders every thread's slab-partial stores before thread 0's
+  // release; its acquire orders the last CTA's reads after the other CTAs' stores
+  __syncthreads();
+  if (tid == 0) last_s = ptx::atom_add_acq_rel_gpu(p.count + b * HM + h, 1) == p.nslab - 1;
+  __syncthreads();
+  if (!last_s) return;
+  const float* ob_part = p.opart + ((size_t)b * HM + h) * p.nslab * p.DV;
+  T* ob = static_cast<T*>(p.out) + b * p.o_s[0] + h * p.o_s[1];
+  for (int d = tid; d < p.DV; d += MX_COLS) {
+    float y = 0.f;
+    for (int k = 0; k < p.nslab; ++k) y += __ldcg(ob_part + (size_t)k * p.DV + d);
+    st(ob + (int64_t)d * p.o_s[2], y);
   }
 }
 
@@ -644,13 +654,19 @@ int device_sms() {
   return n > 0 ? n : 148;
 }
 
-size_t ws_bytes(int B, int L, int KVL) {
+int num_slabs(int KVL) { return (KVL + MX_COLS - 1) / MX_COLS; }
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// workspace: q_lat | split partials | out slab partials | counters
+size_t ws_bytes(int B, int L, int KVL, int DV) {
   int ns, tpc;
   plan(B, L, device_sms(), &ns, &tpc);
   const size_t qlat = (size_t)B * HM * KVL * 4;
   const size_t part = (size_t)B * ns * HM * (KVL + 2) * 4;
-  const size_t mix = (size_t)B * HM * KVL * 4;
-  return ((qlat + 255) / 256) * 256 + ((part + 255) / 256) * 256 + mix;
+  const size_t opart = (size_t)B * HM * num_slabs(KVL) * DV * 4;
+  const size_t count = (size_t)B * HM * 4;
+  return align256(qlat) + align256(part) + align256(opart) + count;
 }
 
 bool kvl_ok(int kvl) { return kvl == 64 || kvl == 128 || kvl == 256 || kvl == 512; }
@@ -672,7 +688,7 @@ int validate(const MlaDecodeArgs* a) {
   if (reinterpret_cast<uintptr_t>(a->workspace) % 256 ||
       reinterpret_cast<uintptr_t>(a->pos) % 8)
     return KDA_ERR_ALIGNMENT;
-  if (a->workspace_bytes < ws_bytes(a->B, a->L, a->KVL)) return KDA_ERR_WORKSPACE;
+  if (a->workspace_bytes < ws_bytes(a->B, a->L, a->KVL, a->DV)) return KDA_ERR_WORKSPACE;
   return KDA_OK;
 }
 
@@ -719,12 +735,7 @@ cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s
     default: e = launch_attn<T, 512>(p, tm, s); break;
   }
   if (e != cudaSuccess) return e;
-  e = launch_dependent(mla_mix_kernel<T>, dim3((p.KVL + MX_COLS - 1) / MX_COLS, p.H, p.B),
-                       MX_COLS, 0, s, p);
-  if (e != cudaSuccess) return e;
-  const size_t osm = (size_t)OUT_BB * p.KVL * sizeof(float);
-  return launch_dependent(mla_out_kernel<T>, dim3(p.H, (p.DV + OUT_ROWS - 1) / OUT_ROWS), 256,
-                          osm, s, p);
+  return launch_dependent(mla_mixout_kernel<T>, dim3(p.nslab, p.H, p.B), MX_COLS, 0, s, p);
 }
 
 }  // namespace
@@ -745,8 +756,8 @@ int read_device_error(bool clear) {
 extern "C" {
 
 size_t mla_decode_workspace_bytes(const MlaDecodeArgs* a) {
-  if (a == nullptr || a->B < 1 || a->L < 1 || !kda::mla::kvl_ok(a->KVL)) return 0;
-  return kda::mla::ws_bytes(a->B, a->L, a->KVL);
+  if (a == nullptr || a->B < 1 || a->L < 1 || a->DV < 1 || !kda::mla::kvl_ok(a->KVL)) return 0;
+  return kda::mla::ws_bytes(a->B, a->L, a->KVL, a->DV);
 }
 
 size_t mla_decode_args_size(void) { return sizeof(MlaDecodeArgs); }
@@ -773,12 +784,15 @@ int mla_decode_fwd(const MlaDecodeArgs* a, void* stream) {
   p.w_vec = a->w_stride[1] == 1 && reinterpret_cast<uintptr_t>(a->w) % 16 == 0 &&
             (a->w_stride[0] * 2) % 16 == 0;
   plan(p.B, p.L, device_sms(), &p.nsplit, &p.tiles_per_cta);
+  p.nslab = num_slabs(p.KVL);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
-  const size_t qlat = (size_t)p.B * HM * p.KVL * 4;
   p.qlat = reinterpret_cast<float*>(ws);
-  p.part = reinterpret_cast<float*>(ws + ((qlat + 255) / 256) * 256);
-  const size_t part_b = (size_t)p.B * p.nsplit * HM * (p.KVL + 2) * 4;
-  p.mix = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.part) + ((part_b + 255) / 256) * 256);
+  ws += align256((size_t)p.B * HM * p.KVL * 4);
+  p.part = reinterpret_cast<float*>(ws);
+  ws += align256((size_t)p.B * p.nsplit * HM * (p.KVL + 2) * 4);
+  p.opart = reinterpret_cast<float*>(ws);
+  ws += align256((size_t)p.B * HM * p.nslab * p.DV * 4);
+  p.count = reinterpret_cast<int*>(ws);
   // kv_buf [B, L, KVL] as a 3-D tensor map: boxes of 64 channels x 64 positions
   EncodeTiled enc = encode_tiled();
   if (enc == nullptr) return KDA_ERR_LAUNCH;

@@ -144,6 +144,14 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// atomic add with acquire-release semantics at device scope; returns the old value
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // programmatic dependent launch: wait until the preceding grid has completed
 // and its writes are visible / let the next grid start launching.  Both are
 // no-ops for a kernel launched without the programmatic-serialization attribute.

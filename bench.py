@@ -479,7 +479,8 @@ def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
 def profile_case(which, reps=3):
     """Three calls of one workload on cuda:0 (the target of the ncu captures
     summarised under profiles/): ``prefill`` = configs[1], ``decode`` = one
-    configs[2] step."""
+    configs[2] step, ``mla`` = one configs[4] MLA decode step (8192-token
+    prompt in the static buffer)."""
     import torch
     kb = importlib.import_module("-kimi-linear-_b200")
     kb.load_library()
@@ -489,6 +490,18 @@ def profile_case(which, reps=3):
         for _ in range(reps):
             kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=CFG1["C"],
                              state_dtype=torch.float32)
+    elif which == "mla":
+        c = CFG4_MLA
+        B, L, H, KVL, DN, DV = c["B"], c["L"], c["H"], c["KVL"], c["DN"], c["DV"]
+        g = torch.Generator(device=dev).manual_seed(11)
+        w = torch.randn(H * (DN + DV), KVL, generator=g, device=dev).mul_(KVL ** -0.5).half()
+        q = torch.randn(B, 1, H, DN, generator=g, device=dev).mul_(0.5).half()
+        ck = torch.randn(B, 1, KVL, generator=g, device=dev).half()
+        buf = torch.zeros(B, L, KVL, device=dev, dtype=torch.float16)
+        buf[:, :c["prompt"]].copy_(torch.randn(B, c["prompt"], KVL, generator=g, device=dev))
+        pos = torch.tensor([c["prompt"]], dtype=torch.int64, device=dev)
+        for _ in range(reps):
+            kb.mla.mla_decode_core(q, ck, buf, pos, w, H, DN, DV, DN ** -0.5)
     else:
         y = kb.synth.make_inputs(CFG2["B"], 1, CFG2["H"], CFG2["K"], CFG2["V"],
                                  dtype=torch.float16, seed=2, s0_std=0.02, device=dev)
@@ -511,7 +524,7 @@ def main():
     ap.add_argument("--mla-steps", type=int, default=128,
                     help="timed steps of the configs[4] MLA decode leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=("prefill", "decode"),
+    ap.add_argument("--case", choices=("prefill", "decode", "mla"),
                     help="profiling target: run the workload three times, print nothing timed")
     a = ap.parse_args()
     if a.case:

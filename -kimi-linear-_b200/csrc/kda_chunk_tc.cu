@@ -253,6 +253,7 @@ template <typename TIO, int LOAD>
 __global__ void __launch_bounds__(PREP_THREADS, 1)
 prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant__ PrepMaps tm) {
   constexpr bool VEC = LOAD >= 1;
+  ptx::grid_dep_launch();          // the state pass may start launching (it waits for this grid)
   extern __shared__ __align__(1024) uint8_t sm[];
   uint8_t* img = sm + P_IMG;
   uint8_t* A2 = sm + P_A2;
@@ -915,6 +916,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
 
   // thread 64 (the copy issuer): stages with a bulk copy in flight and their phase parity
   uint32_t pending = 0, pend_par = 0;
+  ptx::grid_dep_wait();               // the prep grid's chunk images are complete
   if (tid == 64) {
     for (int sg = 0; sg < NST && sg < NT; ++sg) {
       fetch_chunk<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
@@ -1192,12 +1194,6 @@ state_mma_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
   // with a copy in flight and their phase parity
   const bool issuer = tid == MMA_STATE_WARPS * 32 - 32;
   uint32_t pending = 0, pend_par = 0;
-  if (issuer) {
-    for (int sg = 0; sg < NST && sg < NT; ++sg) {
-      fetch_chunk_mma<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
-      pending |= 1u << sg;
-    }
-  }
 
   // chain warps: master state, accumulator layout S[mt][nt] rows
   // KR + 16 mt + gid (+8), columns 8 nt + 2 tig (+1)
@@ -1217,6 +1213,13 @@ state_mma_kernel(const ChunkParams p, const uint8_t* __restrict__ ws) {
         }
         S[mt][nt][e] = x;
       }
+  ptx::grid_dep_wait();               // the prep grid's chunk images are complete
+  if (issuer) {
+    for (int sg = 0; sg < NST && sg < NT; ++sg) {
+      fetch_chunk_mma<VS>(sm + sg * Cfg::STAGE, wsh + (size_t)sg * IMG_BYTES, v0, &full[sg]);
+      pending |= 1u << sg;
+    }
+  }
 
   bool aborted = false;
 #pragma unroll 1
@@ -1379,8 +1382,8 @@ cudaError_t launch_state(const ChunkParams& p, const uint8_t* ws, cudaStream_t s
                                        StateCfg<VS>::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.V / VS, p.H, p.B);
-  kern<<<grid, 128, StateCfg<VS>::SMEM, s>>>(p, ws);
-  return cudaGetLastError();
+  // programmatic dependent of the prep grid: set-up and S0 loads overlap its tail
+  return launch_dependent(kern, grid, 128, StateCfg<VS>::SMEM, s, p, ws);
 }
 
 template <typename TIO, typename TSI, typename TSO, int VS>
@@ -1390,8 +1393,8 @@ cudaError_t launch_state_mma(const ChunkParams& p, const uint8_t* ws, cudaStream
                                        MmaStateCfg<VS>::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.V / VS, p.H, p.B);
-  kern<<<grid, MMA_STATE_WARPS * 32, MmaStateCfg<VS>::SMEM, s>>>(p, ws);
-  return cudaGetLastError();
+  // programmatic dependent of the prep grid: set-up and S0 loads overlap its tail
+  return launch_dependent(kern, grid, MMA_STATE_WARPS * 32, MmaStateCfg<VS>::SMEM, s, p, ws);
 }
 
 // which state pass runs: the register-resident one (true) or the TMEM one

@@ -2,6 +2,9 @@
 #pragma once
 
 #include <cuda.h>   // CUtensorMap and its enums (header only)
+#include <cuda_runtime.h>
+
+#include <utility>
 
 #include "kda_common.cuh"
 
@@ -14,6 +17,26 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiled encode_tiled();
+
+// Launch with programmatic stream serialization: the grid may start while the
+// previous kernel on the stream is still running (once all of that kernel's
+// CTAs have executed griddepcontrol.launch_dependents, or exited); it must
+// execute griddepcontrol.wait before touching anything that kernel writes.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*k)(Params...), dim3 grid, int threads, size_t smem,
+                             cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
 
 namespace mla {
 int read_device_error(bool clear);   // the MLA kernels' error word (mla_decode.cu)

@@ -692,26 +692,6 @@ int validate(const MlaDecodeArgs* a) {
   return KDA_OK;
 }
 
-// launch with programmatic stream serialization: the grid may start while the
-// previous kernel on the stream is still running (after all of that kernel's
-// CTAs have called griddepcontrol.launch_dependents); it calls
-// griddepcontrol.wait before touching anything that kernel writes
-template <typename... Params, typename... Args>
-cudaError_t launch_dependent(void (*k)(Params...), dim3 grid, int threads, size_t smem,
-                             cudaStream_t s, Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
-}
-
 template <typename T, int KVL>
 cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
   auto k = mla_attn_kernel<T, KVL>;

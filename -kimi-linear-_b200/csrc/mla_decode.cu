@@ -403,13 +403,15 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
 #pragma unroll
       for (int off = 1; off < 8; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
       const float m_new = fmaxf(m_run, mt);
-      const float a = (m_new == -INFINITY) ? 1.f : expf(m_run - m_new);
+      // __expf (ex2.approx based, ~1e-6 relative here): p is rounded to the
+      // buffer dtype right after, which dominates the error by far
+      const float a = (m_new == -INFINITY) ? 1.f : __expf(m_run - m_new);
       float ls = 0.f;
       uint32_t pk[4];
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {
-        const float e0 = (v[i] == -INFINITY) ? 0.f : expf(v[i] - m_new);
-        const float e1 = (v[i + 1] == -INFINITY) ? 0.f : expf(v[i + 1] - m_new);
+        const float e0 = (v[i] == -INFINITY) ? 0.f : __expf(v[i] - m_new);
+        const float e1 = (v[i + 1] == -INFINITY) ? 0.f : __expf(v[i + 1] - m_new);
         ls += e0 + e1;
         pk[i / 2] = MmaT<T>::pack(e0, e1);
       }

@@ -18,7 +18,7 @@
 //    CTAs of head h also write batch row h's new latent row at pos;
 //  * mla_attn_kernel: flash decoding.  One CTA per (split, b) walks 64-position
 //    tiles of kv_buf[b] (tiles past pos are not loaded), three TMA stages with a
-//    128-byte swizzle.  Scores: f16/bf16 mma.sync with q_lat split into hi + lo
+//    128-byte swizzle, the first tile requested ahead of the others.  Scores: f16/bf16 mma.sync with q_lat split into hi + lo
 //    parts (fp32-level scores against exact buffer values), K split over the
 //    four warps and summed in shared memory; online softmax in fp32; mixing
 //    P . tile with N split over the warps.  Writes (max, sum, acc) partials;
@@ -285,25 +285,22 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
     for (int g = 0; g < C::GROUPS; ++g)
       ptx::tma_load_3d(sm + stage * C::TILE + g * TS * 128, &tm, 64 * g, t * TS, b, &full[stage]);
   };
-  // Only the tile holding pos is written by the q_lat grid (the new latent
-  // row): the other first-stage tiles load while that grid is still running.
+  // The first tile is requested alone and the other first-stage tiles once it
+  // has landed: with every CTA asking for all of its stages at once, the
+  // first tiles share HBM with the later ones and compute starts late.  Only
+  // the tile holding pos is written by the q_lat grid (the new latent row), so
+  // unless it is that tile the first one loads while that grid still runs.
   uint32_t pending = 0, pend_par = 0;
   const int pos_tile = last / TS;
-  if (tid == 0) {
-    for (int i = 0; i < NST && t_beg + i < t_end; ++i) {
-      if (t_beg + i == pos_tile) continue;
-      fetch(t_beg + i, i);
-      pending |= 1u << i;
-    }
+  if (tid == 0 && t_beg < t_end && t_beg != pos_tile) {
+    fetch(t_beg, 0);
+    pending |= 1u;
   }
   ptx::grid_dep_wait();                               // q_lat and kv_buf[., pos] visible
-  if (tid == 0) {
-    const int i = pos_tile - t_beg;
-    if (i >= 0 && i < NST && pos_tile < t_end) {
-      ptx::fence_proxy_async_global();
-      fetch(pos_tile, i);
-      pending |= 1u << i;
-    }
+  if (tid == 0 && t_beg < t_end && t_beg == pos_tile) {
+    ptx::fence_proxy_async_global();
+    fetch(t_beg, 0);
+    pending |= 1u;
   }
 
   // q_lat of this warp's channel range as hi / lo A fragments
@@ -336,10 +333,18 @@ mla_attn_kernel(const MlaParams p, const __grid_constant__ CUtensorMap tm) {
   for (int t = t_beg; t < t_end; ++t, ++k) {
     const int stage = k % NST;
     const uint8_t* tile = sm + stage * C::TILE;
-    if (ptx::mbar_wait(&full[stage], (k / NST) & 1, kWaitNs)) {
+    const bool landed = ptx::mbar_wait(&full[stage], (k / NST) & 1, kWaitNs);
+    if (landed) {
       if (tid == 0) pending &= ~(1u << stage);
     } else {
       *abort_flag = 1;
+    }
+    if (k == 0 && tid == 0 && landed) {               // the rest of the first stages
+      ptx::fence_proxy_async_global();
+      for (int i = 1; i < NST && t_beg + i < t_end; ++i) {
+        fetch(t_beg + i, i);
+        pending |= 1u << i;
+      }
     }
     // ---- scores: this warp's KW channels, all 64 positions
     float sc[8][4];

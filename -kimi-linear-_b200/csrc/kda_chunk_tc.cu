@@ -275,48 +275,63 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int NT = gridDim.x;
+  const float s = p.scale;
+  // chunk images in linear order n + NT (h + H b) (the workspace order).  The
+  // TMA-input instantiation is persistent (one CTA per SM walks every
+  // stride-th chunk); the others run one chunk per CTA over an (NT, H, B) grid.
+  const int NT = (p.T + CH - 1) / CH;
+  const int total = NT * p.H * p.B;                   // < 2^31 (checked on the host)
+  const int stride = gridDim.x * gridDim.y * gridDim.z;
+  int chunk = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  // the four input boxes of chunk c into the staging region (thread 32; rows
+  // past T arrive as zeros)
+  auto issue_inputs = [&](int c) {
+    const int n2 = c % NT, h2 = (c / NT) % p.H, b2 = c / (NT * p.H);
+    uint8_t* stg = sm + P_STG;
+    ptx::mbar_arrive_expect_tx(tbar, 3 * CH * KD * sizeof(TIO) + STG_BYTES_G);
+    ptx::tma_load_4d(stg, &tm.q, 0, h2, n2 * CH, b2, tbar);
+    ptx::tma_load_4d(stg + CH * KD * sizeof(TIO), &tm.k, 0, h2, n2 * CH, b2, tbar);
+    ptx::tma_load_4d(stg + 2 * CH * KD * sizeof(TIO), &tm.v, 0, h2, n2 * CH, b2, tbar);
+    ptx::tma_load_4d(stg + 3 * CH * KD * sizeof(TIO), &tm.g, 0, h2, n2 * CH, b2, tbar);
+  };
+
+  // the first chunk's input copies go first
+  if (tid == 32) {
+    ptx::mbar_init(mbar, 1);
+    if constexpr (LOAD == 3) ptx::mbar_init(tbar, 1);
+    ptx::fence_mbar_init();
+    if constexpr (LOAD == 3) {
+      if (chunk < total) issue_inputs(chunk);
+    }
+  }
+  if (warp == 0) {                  // TMEM for phase 5 (one CTA per SM: never contended)
+    ptx::tmem_alloc(tslot, kPrepTmemCols);
+    ptx::tmem_relinquish();
+    ptx::tc_fence_before();
+  }
+
+#pragma unroll 1
+  for (uint32_t it = 0; chunk < total; chunk += stride, ++it) {
+  const int n = chunk % NT, h = (chunk / NT) % p.H, b = chunk / (NT * p.H);
   const int t0 = n * CH;
   const int nvalid = min(CH, p.T - t0);
-  const float s = p.scale;
   const TIO* qb = static_cast<const TIO*>(p.q) + b * p.q_s[0] + h * p.q_s[2];
   const TIO* kb = static_cast<const TIO*>(p.k) + b * p.k_s[0] + h * p.k_s[2];
   const TIO* vb = static_cast<const TIO*>(p.v) + b * p.v_s[0] + h * p.v_s[2];
   const float* gb = p.g + b * p.g_s[0] + h * p.g_s[2];
   const float* bb = p.beta + b * p.b_s[0] + h * p.b_s[2];
 
-  // the input copies go first; beta waits in a register until they landed
-  // (its load latency then overlaps theirs) and reaches shared memory with
-  // the phase-1 barrier
-  if (tid == 32) {
-    ptx::mbar_init(mbar, 1);
-    if constexpr (LOAD == 3) ptx::mbar_init(tbar, 1);
-    ptx::fence_mbar_init();
-    if constexpr (LOAD == 3) {      // rows past T arrive as zeros
-      uint8_t* stg = sm + P_STG;
-      ptx::mbar_arrive_expect_tx(tbar, 3 * CH * KD * sizeof(TIO) + STG_BYTES_G);
-      ptx::tma_load_4d(stg, &tm.q, 0, h, t0, b, tbar);
-      ptx::tma_load_4d(stg + CH * KD * sizeof(TIO), &tm.k, 0, h, t0, b, tbar);
-      ptx::tma_load_4d(stg + 2 * CH * KD * sizeof(TIO), &tm.v, 0, h, t0, b, tbar);
-      ptx::tma_load_4d(stg + 3 * CH * KD * sizeof(TIO), &tm.g, 0, h, t0, b, tbar);
-    }
-  }
+  // beta waits in a register until the inputs landed (its load latency then
+  // overlaps theirs) and reaches shared memory with the phase-1 barrier
   if (tid < 16) steep[tid] = 0u;
   const float beta_c = (tid < nvalid) ? bb[(int64_t)(t0 + min(tid, CH - 1)) * p.b_s[1]] : 0.f;
-  if (warp == 0) {                  // TMEM for phase 5 (one CTA per SM: never contended)
-    ptx::tmem_alloc(tslot, kPrepTmemCols);
-    ptx::tmem_relinquish();
-    ptx::tc_fence_before();
-  }
-  uint8_t* img_g = ws + ((size_t)(b * p.H + h) * NT + n) * IMG_BYTES;
 
-  // L2 prefetch of the inputs of the chunk one SM-count further in launch
-  // order: with one CTA per SM that is about the CTA that starts on this SM
-  // when this one retires, so its loads hit L2 instead of HBM.
+  // L2 prefetch of inputs a chunk period ahead: the next chunk of this CTA
+  // (persistent; its copies are issued after phase 3 and then hit L2), or the
+  // chunk one SM-count further in launch order (the CTA that starts on this
+  // SM when this one retires).
   {
-    const long total = (long)NT * p.H * p.B;
-    const long tgt = n + (long)NT * (h + (long)p.H * b) + ptx::num_sms();
+    const long tgt = LOAD == 3 ? (long)chunk + stride : (long)chunk + ptx::num_sms();
     if (tgt < total) {
       const int n2 = (int)(tgt % NT), h2 = (int)((tgt / NT) % p.H), b2 = (int)(tgt / ((long)NT * p.H));
       if constexpr (LOAD == 3) {                   // four box prefetches
@@ -374,12 +389,12 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
   // gr[8] is the row after the half (next half or next block)
   float2 gr[9], qr[8], kr[8], vr[8];
   if constexpr (LOAD == 3) {
-    __syncthreads();                                 // tbar initialised
-    const bool in_ok = ptx::mbar_wait(tbar, 0, kWaitNs);
+    __syncthreads();                                 // tbar initialised, steep reset
+    const bool in_ok = ptx::mbar_wait(tbar, it & 1u, kWaitNs);
     if (__syncthreads_or(!in_ok)) {                  // the copies never landed: give up
       if (tid == 32) {
         atomicExch(&g_kda_device_error, 3);
-        ptx::mbar_wait(tbar, 0, kWaitNs / 2);        // let them land before smem is released
+        ptx::mbar_wait(tbar, it & 1u, kWaitNs / 2);  // let them land before smem is released
       }
       __syncthreads();
       if (warp == 0) {
@@ -526,7 +541,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
   ptx::fence_proxy_async_smem();
   __syncthreads();
   if (tid == 0) {              // Kbar^T and d are final: [IMG_A3, IMG_SHARED) leaves now
-    ptx::bulk_s2g(img_g + IMG_A3, img + IMG_A3, IMG_SHARED - IMG_A3);
+    ptx::bulk_s2g(ws + (size_t)chunk * IMG_BYTES + IMG_A3, img + IMG_A3, IMG_SHARED - IMG_A3);
     ptx::bulk_commit();
   }
 
@@ -698,7 +713,13 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
     st_h2(A2, a2_off(row, col), Mm[row * LMP + col] * sbeta[col],
           Mm[row * LMP + col + 1] * sbeta[col + 1]);
   }
+  // the staging region (inputs, then the phase-1..3 operands) is dead from
+  // here on: the next chunk's copies land in it while phases 4-5 run
+  if constexpr (LOAD == 3) ptx::fence_proxy_async_smem();
   __syncthreads();
+  if constexpr (LOAD == 3) {
+    if (tid == 32 && chunk + stride < total) issue_inputs(chunk + stride);
+  }
 
   // ---- 4. AM = Aout M over Aout (rows 64-127 of A2) -------------------------
   // Aout M is block lower triangular like M: with it, one GEMM gives W, U,
@@ -747,14 +768,16 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
     }
     __syncwarp();
   }
-  const bool mma_ok = ptx::mbar_wait(mbar, 0, kWaitNs);
+  const bool mma_ok = ptx::mbar_wait(mbar, it & 1u, kWaitNs);
   ptx::tc_fence_after();
   if (__syncthreads_or(!mma_ok)) {                       // the GEMM never finished: give up
     if (tid == 0) {
       atomicExch(&g_kda_device_error, 2);
-      ptx::mbar_wait(mbar, 0, kWaitNs / 2);
+      ptx::mbar_wait(mbar, it & 1u, kWaitNs / 2);
       ptx::bulk_wait_read();
     }
+    if (LOAD == 3 && tid == 32 && chunk + stride < total)   // the next chunk's copies in flight
+      ptx::mbar_wait(tbar, (it + 1u) & 1u, kWaitNs / 2);
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -799,18 +822,23 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, const __grid_constant
         } else {                                           // U, F
           off = row < 64 ? IMG_U + vb_off(row, col) : IMG_F + vb_off(row - 64, col);
         }
-        *reinterpret_cast<uint4*>(img_g + off) =
+        *reinterpret_cast<uint4*>(ws + (size_t)chunk * IMG_BYTES + off) =
             make_uint4(pack_h2(x[0], x[1]), pack_h2(x[2], x[3]), pack_h2(x[4], x[5]),
                        pack_h2(x[6], x[7]));
       }
     }
   }
+  // end of the chunk: TMEM read out, and the Kbar^T / d store must have read
+  // shared memory before the next chunk's phase 1 rewrites the image region
   ptx::tc_fence_before();
   __syncthreads();
-  if (tid == 0) ptx::bulk_wait_read();   // the Kbar^T / d store must have read smem
+  if (tid == 0) ptx::bulk_wait_read();
+  __syncthreads();
+  ptx::tc_fence_after();
+  }  // chunk loop
+
   if (warp == 0) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tbase, kPrepTmemCols);
+    ptx::tmem_dealloc(*tslot, kPrepTmemCols);
   }
 }
 
@@ -1410,6 +1438,13 @@ cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s,
   if (e != cudaSuccess) return e;
   const int NT = (p.T + CH - 1) / CH;
   dim3 pgrid(NT, p.H, p.B);
+  if constexpr (LOAD == 3) {        // persistent: one CTA per SM walks the chunks
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long total = (long)NT * p.H * p.B;
+    pgrid = dim3((unsigned)(total < sms ? total : sms), 1, 1);
+  }
   prep<<<pgrid, PREP_THREADS, PREP_SMEM, s>>>(p, ws, maps);
   return cudaGetLastError();
 }

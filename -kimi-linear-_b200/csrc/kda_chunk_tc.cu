@@ -1437,6 +1437,7 @@ cudaError_t launch_prep(const ChunkParams& p, uint8_t* ws, cudaStream_t s,
                                        PREP_SMEM);
   if (e != cudaSuccess) return e;
   const int NT = (p.T + CH - 1) / CH;
+  if ((long long)NT * p.H * p.B > 0x7fffffffLL) return cudaErrorInvalidValue;   // int chunk index
   dim3 pgrid(NT, p.H, p.B);
   if constexpr (LOAD == 3) {        // persistent: one CTA per SM walks the chunks
     int dev = 0, sms = 148;

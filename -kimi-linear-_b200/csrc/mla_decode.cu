@@ -11,9 +11,10 @@
 //   out[b, h]      = mixed[b, h] W_v[h]^T                         (fp32, then I/O dtype)
 //   pos           += 1
 // Three kernels on the caller's stream, reading `pos` from device memory
-// (graph-capturable).  The last two are launched as programmatic dependents
-// of the one before (launch, barrier set-up, the tile loads that do not need
-// the previous kernel's output and the W_v loads overlap its tail):
+// (graph-capturable).  All three are launched as programmatic dependents of
+// the kernel before them (launch, barrier set-up, the tile loads that do not
+// need the previous kernel's output and the W_v loads overlap its tail; the
+// first waits before any read, since its inputs come from whatever precedes it):
 //  * mla_qlat_kernel: q_lat in fp32 (one CTA per (h, 64-channel slab)); the
 //    CTAs of head h also write batch row h's new latent row at pos;
 //  * mla_attn_kernel: flash decoding.  One CTA per (split, b) walks 64-position
@@ -150,6 +151,10 @@ mla_qlat_kernel(const MlaParams p) {
   const int h = blockIdx.x, c0 = blockIdx.y * QL_COLS, tid = threadIdx.x;
   const int chunk = tid & 7, dsub = tid >> 3;
   const int ncols = min(QL_COLS, p.KVL - c0);         // KVL = 64: half a slab
+  // launched as a programmatic dependent of whatever precedes it on the stream
+  // (q_nope and c_kv come from it, pos from the previous step's merge grid):
+  // nothing is read before the wait
+  ptx::grid_dep_wait();
   ptx::grid_dep_launch();                             // the attention grid may start launching
   if (blockIdx.y == 0)                                // slab-partial counters of this call
     for (int b = tid; b < p.B; b += blockDim.x) p.count[b * HM + h] = 0;
@@ -520,6 +525,7 @@ mla_mixout_kernel(const MlaParams p) {
     if (wpre && 8 * j < ncols)
       wr[j] = *reinterpret_cast<const uint4*>(wv + (int64_t)tid * p.w_s[0] + c0 + 8 * j);
   ptx::grid_dep_wait();                               // the attention partials are visible
+  ptx::grid_dep_launch();                             // a following dependent grid may launch
   if (slab == 0 && h == 0 && b == 0 && tid == 0) *p.pos += 1;   // its readers have finished
 
   const float* pb = p.part + ((size_t)b * ns * HM + h) * (KVL + 2);
@@ -710,10 +716,12 @@ cudaError_t launch_attn(const MlaParams& p, const CUtensorMap& tm, cudaStream_t 
 
 template <typename T>
 cudaError_t launch_all(const MlaParams& p, const CUtensorMap& tm, cudaStream_t s) {
-  // the first kernel follows foreign work on the stream: an ordinary launch
+  // programmatic dependent too: it waits for the preceding kernel before its
+  // first read, and its launch overlaps that kernel's tail when the kernel
+  // triggers early (the previous step's merge grid does)
   const size_t qsm = (size_t)QL_RG * QL_BB * QL_COLS * sizeof(float);
-  mla_qlat_kernel<T><<<dim3(HM, (p.KVL + QL_COLS - 1) / QL_COLS), 256, qsm, s>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_dependent(mla_qlat_kernel<T>, dim3(HM, (p.KVL + QL_COLS - 1) / QL_COLS),
+                                   256, qsm, s, p);
   if (e != cudaSuccess) return e;
   switch (p.KVL) {
     case 64: e = launch_attn<T, 64>(p, tm, s); break;

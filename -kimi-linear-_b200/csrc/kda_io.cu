@@ -21,6 +21,8 @@
 // Rounding follows the reference's fp16/bf16 path: the conv output, the SiLU
 // output and the RMSNorm output are rounded to the I/O dtype where the
 // reference materialises them in that dtype; reductions are fp32.
+#include <type_traits>
+
 #include "kda_internal.cuh"
 
 namespace kda {
@@ -144,6 +146,195 @@ prologue_kernel(const PrologueParams p) {
   }
 }
 
+// 8 consecutive values from a 16-byte-aligned address as fp32 / 8 fp32 values
+// stored as T (round to nearest) at a 16-byte-aligned address
+template <typename T>
+__device__ __forceinline__ void ld8v(const T* ptr, float (&x)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(ptr);
+    const float4 c = *reinterpret_cast<const float4*>(ptr + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(ptr);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f;
+      if constexpr (std::is_same<T, __half>::value)
+        f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __half>::value) {
+      const __half2 hv = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+    } else {
+      const __nv_bfloat162 hv = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+  }
+  *reinterpret_cast<uint4*>(ptr) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The same prologue for 16-bit I/O with 16-byte-aligned rows (what the module
+// passes), head dim HD in {32, 64, 128}: a thread owns 8 adjacent channels of
+// a run of TPT tokens plus the three rows before them (the conv window), so
+// every global access is 16 bytes per thread -- the thread-per-channel kernel
+// above issues 2-byte accesses, 64 bytes per warp request, and the SM's limit
+// on outstanding requests caps it near 0.6 TB/s.  Tiles of TTV = 32 tokens
+// (fewer registers per thread, more CTAs per SM).  Same rounding points; SiLU
+// uses the fast exponential and divide, whose ~1e-6 relative error vanishes
+// in the rounding of its output to the 16-bit I/O type.
+constexpr int TTV = 32;   // tokens per vectorised prologue CTA
+
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+
+template <typename TIO, typename TG, int HD>
+__global__ void __launch_bounds__(128)
+prologue_vec_kernel(const PrologueParams p) {
+  constexpr int CG = HD / 8, TGRP = 128 / CG, TPT = TTV / TGRP;
+  static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
+  __shared__ __align__(16) float ys[TTV][HD + 4];
+  __shared__ float rstd[TTV];
+  const int tid = threadIdx.x, cg = tid % CG, tg = tid / CG;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int tensor = blockIdx.y / p.H, h = blockIdx.y - tensor * p.H;
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * TTV;
+  const int nt = min(TTV, p.T - t0);
+  const int i0 = tg * TPT;                         // first token of this thread in the tile
+
+  if (tensor == 3) {                               // decay and beta gates
+    const int ch0 = h * p.K + 8 * cg;
+    float a[8], dtb[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      a[e] = -expf(p.A_log[ch0 + e]);
+      dtb[e] = p.dt_bias[ch0 + e];
+    }
+    const TG* gk = static_cast<const TG*>(p.gk) + b * p.gk_s[0] + ch0;
+    float* g = p.g + b * p.g_s[0] + h * p.g_s[2] + 8 * cg;
+    float gv[TPT][8];
+#pragma unroll
+    for (int i = 0; i < TPT; ++i)
+      if (i0 + i < nt) ld8v(gk + (int64_t)(t0 + i0 + i) * p.gk_s[1], gv[i]);
+#pragma unroll
+    for (int i = 0; i < TPT; ++i) {
+      if (i0 + i >= nt) break;
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = a[e] * softplus(gv[i][e] + dtb[e]);
+      float* gr = g + (int64_t)(t0 + i0 + i) * p.g_s[1];
+      *reinterpret_cast<float4*>(gr) = make_float4(y[0], y[1], y[2], y[3]);
+      *reinterpret_cast<float4*>(gr + 4) = make_float4(y[4], y[5], y[6], y[7]);
+    }
+    for (int i = tid; i < nt; i += blockDim.x) {       // beta: every token of the tile
+      const int t = t0 + i;
+      const TG* bl = static_cast<const TG*>(p.beta_logit) + b * p.bl_s[0] + (int64_t)t * p.bl_s[1] + h;
+      p.beta[b * p.beta_s[0] + (int64_t)t * p.beta_s[1] + h] = sigmoidf(ld(bl));
+    }
+    return;
+  }
+
+  const int D = tensor == 2 ? p.H * p.V : p.H * p.K;
+  const int ch0 = h * HD + 8 * cg;
+  const TIO* x = static_cast<const TIO*>(tensor == 0 ? p.q_in : tensor == 1 ? p.k_in : p.v_in) +
+                 b * p.in_s[tensor][0] + ch0;
+  const int64_t xs = p.in_s[tensor][1];
+  const TIO* hist = static_cast<const TIO*>(tensor == 0 ? p.hist_q : tensor == 1 ? p.hist_k : p.hist_v);
+  const TIO* hb = hist ? hist + b * p.hist_bs[tensor] + ch0 : nullptr;
+  const float* w = (tensor == 0 ? p.w_q : tensor == 1 ? p.w_k : p.w_v) + (int64_t)ch0 * p.conv_size;
+  const float* bias = tensor == 0 ? p.b_q : tensor == 1 ? p.b_k : p.b_v;
+  const int cs = p.conv_size, keep = cs - 1;
+
+  // rows t0 + i0 - 3 .. t0 + i0 + TPT - 1, every load issued before any use
+  float xv[TPT + 3][8];
+#pragma unroll
+  for (int r = 0; r < TPT + 3; ++r) {
+    const int i = i0 - 3 + r, t = t0 + i;
+    if (i < nt && t >= 0) {
+      ld8v(x + (int64_t)t * xs, xv[r]);
+    } else if (i < nt && hb != nullptr && t >= -keep) {
+      ld8v(hb + (int64_t)(keep + t) * D, xv[r]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+    }
+  }
+  // taps at the right end of a four-wide window, as in the kernel above
+  float wv[8][4], bv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    bv[e] = bias ? bias[ch0 + e] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wv[e][j] = (j >= 4 - cs) ? w[e * cs + j - (4 - cs)] : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < TPT; ++i) {
+    if (i0 + i >= nt) break;
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float acc = bv[e];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j >= 4 - cs) acc = fmaf(xv[i + j][e], wv[e][j], acc);
+      y[e] = rnd<TIO>(silu_fast(rnd<TIO>(acc)));
+    }
+    *reinterpret_cast<float4*>(&ys[i0 + i][8 * cg]) = make_float4(y[0], y[1], y[2], y[3]);
+    *reinterpret_cast<float4*>(&ys[i0 + i][8 * cg + 4]) = make_float4(y[4], y[5], y[6], y[7]);
+  }
+  // new conv cache: the last keep inputs of cat(history, x)
+  if (p.new_q != nullptr && t0 + nt == p.T && keep > 0 && tg == 0) {
+    TIO* nc = static_cast<TIO*>(tensor == 0 ? p.new_q : tensor == 1 ? p.new_k : p.new_v) +
+              b * (int64_t)keep * D + ch0;
+    for (int j = 0; j < keep; ++j) {
+      const int t = p.T - keep + j;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = t >= 0 ? ld(x + (int64_t)t * xs + e)
+                               : (hb != nullptr ? ld(hb + (int64_t)(keep + t) * D + e) : 0.f);
+        st(nc + (int64_t)j * D + e, v);
+      }
+    }
+  }
+  __syncthreads();
+
+  const bool norm = tensor < 2;
+  if (norm) {                                      // per-token L2 norm over the head
+    for (int i = warp; i < nt; i += 4) {
+      float ss = 0.f;
+      for (int cc = lane; cc < HD; cc += 32) ss = fmaf(ys[i][cc], ys[i][cc], ss);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) rstd[i] = fminf(rsqrtf(ss), 1.f / p.eps);
+    }
+    __syncthreads();
+  }
+  TIO* out = static_cast<TIO*>(tensor == 0 ? p.q : tensor == 1 ? p.k : p.v) +
+             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + 8 * cg;
+  const int64_t os = p.out_s[tensor][1];
+#pragma unroll
+  for (int i = 0; i < TPT; ++i) {
+    if (i0 + i >= nt) break;
+    float y[8];
+    const float r = norm ? rstd[i0 + i] : 1.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = norm ? ys[i0 + i][8 * cg + e] * r : ys[i0 + i][8 * cg + e];
+    st8v(out + (int64_t)(t0 + i0 + i) * os, y);
+  }
+}
+
 // one warp per (b, t, h) row of V channels (V <= 128, multiple of 32)
 template <typename TIO>
 __global__ void __launch_bounds__(256)
@@ -178,14 +369,51 @@ epilogue_kernel(const EpilogueParams p) {
   }
 }
 
+// every address the vectorised prologue touches with 16-byte accesses is
+// 16-byte aligned (pointers and strides; inner strides are 1 by contract)
+static bool vec_ok(const PrologueParams& p, size_t gate_size) {
+  auto al = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  if (!(p.K == p.V && (p.K == 32 || p.K == 64 || p.K == 128))) return false;
+  const void* in[3] = {p.q_in, p.k_in, p.v_in};
+  const void* out[3] = {p.q, p.k, p.v};
+  const void* hist[3] = {p.hist_q, p.hist_k, p.hist_v};
+  for (int t = 0; t < 3; ++t) {
+    if (!al(in[t]) || p.in_s[t][0] % 8 || p.in_s[t][1] % 8) return false;
+    if (!al(out[t]) || p.out_s[t][0] % 8 || p.out_s[t][1] % 8 || p.out_s[t][2] % 8 ||
+        p.out_s[t][3] != 1)
+      return false;
+    if (hist[t] != nullptr && (!al(hist[t]) || p.hist_bs[t] % 8)) return false;
+  }
+  const int64_t gper = 16 / (int64_t)gate_size;
+  if (!al(p.gk) || p.gk_s[0] % gper || p.gk_s[1] % gper) return false;
+  if (!al(p.g) || p.g_s[0] % 4 || p.g_s[1] % 4 || p.g_s[2] % 4 || p.g_s[3] != 1) return false;
+  return true;
+}
+
+template <typename TIO, typename TG>
+static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
+  dim3 grid((p.T + TT - 1) / TT, 4 * p.H, p.B);
+  if constexpr (!std::is_same<TIO, float>::value) {
+    if (vec_ok(p, sizeof(TG))) {
+      const dim3 vgrid((p.T + TTV - 1) / TTV, 4 * p.H, p.B);
+      switch (p.K) {
+        case 32: prologue_vec_kernel<TIO, TG, 32><<<vgrid, 128, 0, s>>>(p); break;
+        case 64: prologue_vec_kernel<TIO, TG, 64><<<vgrid, 128, 0, s>>>(p); break;
+        default: prologue_vec_kernel<TIO, TG, 128><<<vgrid, 128, 0, s>>>(p); break;
+      }
+      return cudaGetLastError();
+    }
+  }
+  const int threads = p.K;   // K == V enforced by the caller
+  prologue_kernel<TIO, TG><<<grid, threads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename TIO>
 static cudaError_t launch_pro_t(const PrologueParams& p, cudaStream_t s) {
-  dim3 grid((p.T + TT - 1) / TT, 4 * p.H, p.B);
-  const int threads = p.K;   // K == V enforced by the caller
-  if (p.gate_dtype == KDA_DTYPE_F32) prologue_kernel<TIO, float><<<grid, threads, 0, s>>>(p);
-  else if (p.gate_dtype == KDA_DTYPE_F16) prologue_kernel<TIO, __half><<<grid, threads, 0, s>>>(p);
-  else prologue_kernel<TIO, __nv_bfloat16><<<grid, threads, 0, s>>>(p);
-  return cudaGetLastError();
+  if (p.gate_dtype == KDA_DTYPE_F32) return launch_pro_g<TIO, float>(p, s);
+  if (p.gate_dtype == KDA_DTYPE_F16) return launch_pro_g<TIO, __half>(p, s);
+  return launch_pro_g<TIO, __nv_bfloat16>(p, s);
 }
 
 }  // namespace io

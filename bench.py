@@ -26,6 +26,8 @@ Reported, all on the device with CUDA events on the launching stream:
                 configs[4] (B=4, buffer 8192 + 256 latents), CUDA graph,
                 against HBM bandwidth (the rest of configs[4], the model
                 around it, cannot run on the GPU box: see DESIGN.md);
+* ``fused_io``  the fused prologue / epilogue kernels of a KDA layer at the
+                configs[1] shape, against HBM bandwidth;
 * ``long_context`` BASELINE configs[3]: B=8, T=32768 bf16 prefill with a
                 fp32 S0, (b, h) sharded over the ranks (strong scaling), with
                 and without the final gather of o and S to rank 0;
@@ -257,6 +259,39 @@ def _events_time(torch, fn, steps, warmup, clk=None, dist=None):
 PREFILL_SETS = 4   # rotating input sets: 4 x 100 MB of inputs, plus outputs, > 3x L2
 
 
+def _graph_time(torch, dev, fn, n, steps, warmup, clk=None):
+    """Mean device ms per call of ``fn(0) .. fn(n-1)`` captured in one CUDA
+    graph (after a warm-up on a side stream, as the decode legs do) and
+    replayed; events bracket every replay."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(n):
+            fn(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(n):
+            fn(i)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, steps // n)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
+    if clk is not None:
+        clk.start()
+    for i in range(reps):
+        starts[i].record()
+        graph.replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    if clk is not None:
+        clk.stop()
+    del graph
+    return sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / (reps * n)
+
+
 def _e2e_pipelined(torch, run, host, outs_h, steps, warmup, clk=None, dist=None, slots=2):
     """End-to-end steps with the PCIe copies of consecutive steps overlapped:
     the H2D of step i + 1 (copy stream, into one of ``slots`` device input
@@ -476,6 +511,56 @@ def bench_mla_decode(torch, kb, dev, steps, warmup, clk):
     return ms, reps * NBUF, nbytes
 
 
+def bench_fused_io(torch, kb, dev, steps, warmup, clk):
+    """The fused prologue (short conv + SiLU + L2 norm of q/k, gates, beta)
+    and epilogue (head RMSNorm x weight x sigmoid gate) of one KDA layer at the
+    configs[1] shape (B=1, T=4096, H=16, K=V=128, fp16, conv size 4 with bias),
+    through ``kda_prologue`` / ``kda_epilogue``.  Four rotating input sets
+    (256 MB and 128 MB, both > L2), one call on each captured in a CUDA graph
+    and replayed (a call's host work is longer than its kernel, so eager
+    timing would measure the host).  Returns (prologue ms, epilogue ms,
+    prologue bytes, epilogue bytes): algorithmic bytes = one read of every
+    input and one write of every output."""
+    B, T, H, K = 1, CFG1["T"], CFG1["H"], CFG1["K"]
+    D, cs = H * K, 4
+    g = torch.Generator(device=dev).manual_seed(5)
+    f16 = torch.float16
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(f16)
+
+    pro = [dict(q=rnd(B, T, D), k=rnd(B, T, D), v=rnd(B, T, D), gk=rnd(B, T, D),
+                beta=rnd(B, T, H)) for _ in range(4)]
+    # conv weights as the module path passes them: its fp32 copies, cast once
+    # per parameter version (fused.projections), so no cast runs per call
+    ws = [(torch.randn(D, 1, cs, generator=g, device=dev) * 0.4).to(f16).float()
+          for _ in range(3)]
+    bs = [(torch.randn(D, generator=g, device=dev) * 0.1).to(f16).float() for _ in range(3)]
+    A_log = torch.log(torch.rand(H, K, generator=g, device=dev) * 15 + 1)
+    dt_bias = torch.log(torch.expm1(torch.rand(H, K, generator=g, device=dev) * 0.099 + 1e-3))
+
+    def prologue(i):
+        x = pro[i % 4]
+        return kb.kda_prologue(x["q"], x["k"], x["v"], x["gk"], x["beta"], ws, bs, A_log,
+                               dt_bias, H, K, K, 1e-6)
+
+    pro_ms = _graph_time(torch, dev, prologue, 4, steps, warmup, clk)
+    del pro
+    epi = [dict(o=rnd(B, T, H, K), og=rnd(B, T, D)) for _ in range(4)]
+    w = torch.rand(H, K, generator=g, device=dev) + 0.5
+
+    def epilogue(i):
+        x = epi[i % 4]
+        return kb.kda_epilogue(x["o"], x["og"], w, 1e-6)
+
+    epi_ms = _graph_time(torch, dev, epilogue, 4, steps, warmup, clk)
+    del epi
+    n = B * T * D
+    pro_bytes = 4 * n * 2 + B * T * H * 2 + 3 * n * 2 + n * 4 + B * T * H * 4
+    epi_bytes = 3 * n * 2
+    return pro_ms, epi_ms, pro_bytes, epi_bytes
+
+
 def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
     """Config 3: B=8, T=32768, H=16 bf16 prefill with a fp32 S0, (b, h)
     sharded over the ranks (strong scaling), then o and S gathered to rank 0.
@@ -586,6 +671,8 @@ def main():
                     help="timed steps of the configs[3] leg (0 skips it)")
     ap.add_argument("--mla-steps", type=int, default=128,
                     help="timed steps of the configs[4] MLA decode leg")
+    ap.add_argument("--io-steps", type=int, default=50,
+                    help="timed calls of the fused prologue / epilogue leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=("prefill", "decode", "mla"),
                     help="profiling target: run the workload three times, print nothing timed")
@@ -645,6 +732,8 @@ def main():
         dec_ms = dec_t.item()
         mla_ms, mla_steps, mla_bytes = bench_mla_decode(torch, kb, dev, a.mla_steps, a.warmup,
                                                         clk)
+        io_ms = bench_fused_io(torch, kb, dev, a.io_steps, a.warmup, clk) \
+            if a.io_steps > 0 else None
         long_ctx = None
         if a.long_steps > 0:
             long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, dist, world,
@@ -725,6 +814,20 @@ def main():
                                         "peak": hbm, "unit": "GB/s",
                                         "frac": mla_bytes / (mla_ms * 1e-3) / 1e9 / hbm,
                                         "algorithmic_bytes": mla_bytes}},
+            "fused_io": None if io_ms is None else {
+                "workload": "fused KDA prologue (conv 4 + SiLU + q/k L2 norm + gates + beta) "
+                            "and epilogue (head RMSNorm x weight x sigmoid gate) at the "
+                            "configs[1] shape, fp16, 4 rotating input sets (> L2), "
+                            "CUDA graph of one call per set, replayed",
+                **{name: {"value": CFG1["T"] / (ms * 1e-3), "unit": "tokens/s",
+                          "ms_per_call": ms,
+                          "roofline": {"bound": "hbm",
+                                       "achieved": nb / (ms * 1e-3) / 1e9,
+                                       "peak": hbm, "unit": "GB/s",
+                                       "frac": nb / (ms * 1e-3) / 1e9 / hbm,
+                                       "algorithmic_bytes": nb}}
+                   for name, ms, nb in (("prologue", io_ms[0], io_ms[2]),
+                                        ("epilogue", io_ms[1], io_ms[3]))}},
             "long_context": long_ctx,
             "gpu_launches": a.steps * launches_per_call,
             "clocks": clocks,

@@ -409,6 +409,59 @@ static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// The epilogue for 16-bit I/O with V = 128 and 8-byte-aligned rows: lane l
+// owns channels 4l .. 4l + 3, one 8-byte access per tensor and row (the kernel
+// above makes four 2-byte accesses, 64 bytes per warp request).
+template <typename TIO>
+__global__ void __launch_bounds__(256)
+epilogue_vec_kernel(const EpilogueParams p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long rows = (long)p.B * p.T * p.H;
+  if (warp >= rows) return;
+  const int h = warp % p.H;
+  const long bt = warp / p.H;
+  const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+  const TIO* o = static_cast<const TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] + h * p.o_s[2];
+  const TIO* og = static_cast<const TIO*>(p.og) + b * p.og_s[0] + (int64_t)t * p.og_s[1] + h * 128;
+  TIO* y = static_cast<TIO*>(p.y) + b * p.y_s[0] + (int64_t)t * p.y_s[1] + h * 128;
+  auto ld4 = [](const TIO* ptr, float (&x)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(ptr);
+    float2 a, c;
+    if constexpr (std::is_same<TIO, __half>::value) {
+      a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      c = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    } else {
+      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    }
+    x[0] = a.x; x[1] = a.y; x[2] = c.x; x[3] = c.y;
+  };
+  float xv[4], gv[4];
+  ld4(o + 4 * lane, xv);
+  ld4(og + 4 * lane, gv);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = fmaf(xv[j], xv[j], ss);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(ss / 128.f + p.eps);
+  const float4 w = *reinterpret_cast<const float4*>(p.weight + h * 128 + 4 * lane);
+  const float wv[4] = {w.x, w.y, w.z, w.w};
+  float out[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = rnd<TIO>(xv[j] * r * wv[j]) * sigmoidf(gv[j]);
+  uint2 u;
+  if constexpr (std::is_same<TIO, __half>::value) {
+    const __half2 a = __floats2half2_rn(out[0], out[1]), c = __floats2half2_rn(out[2], out[3]);
+    u = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&c));
+  } else {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(out[0], out[1]);
+    const __nv_bfloat162 c = __floats2bfloat162_rn(out[2], out[3]);
+    u = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&c));
+  }
+  *reinterpret_cast<uint2*>(y + 4 * lane) = u;
+}
+
 template <typename TIO>
 static cudaError_t launch_pro_t(const PrologueParams& p, cudaStream_t s) {
   if (p.gate_dtype == KDA_DTYPE_F32) return launch_pro_g<TIO, float>(p, s);
@@ -430,10 +483,22 @@ cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s) {
   const long rows = (long)p.B * p.T * p.H;
   const int threads = 256;
   const long blocks = (rows * 32 + threads - 1) / threads;
+  auto al8 = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 8 == 0; };
+  const bool vec = p.io_dtype != KDA_DTYPE_F32 && p.V == 128 && al8(p.o) && al8(p.og) &&
+                   al8(p.y) && reinterpret_cast<uintptr_t>(p.weight) % 16 == 0 &&
+                   p.o_s[0] % 4 == 0 && p.o_s[1] % 4 == 0 && p.o_s[2] % 4 == 0 &&
+                   p.og_s[0] % 4 == 0 && p.og_s[1] % 4 == 0 && p.y_s[0] % 4 == 0 &&
+                   p.y_s[1] % 4 == 0;
   switch (p.io_dtype) {
     case KDA_DTYPE_F32: io::epilogue_kernel<float><<<blocks, threads, 0, s>>>(p); break;
-    case KDA_DTYPE_F16: io::epilogue_kernel<__half><<<blocks, threads, 0, s>>>(p); break;
-    default: io::epilogue_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p); break;
+    case KDA_DTYPE_F16:
+      if (vec) io::epilogue_vec_kernel<__half><<<blocks, threads, 0, s>>>(p);
+      else io::epilogue_kernel<__half><<<blocks, threads, 0, s>>>(p);
+      break;
+    default:
+      if (vec) io::epilogue_vec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p);
+      else io::epilogue_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p);
+      break;
   }
   return cudaGetLastError();
 }

@@ -187,8 +187,9 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 }
 
 // The same prologue for 16-bit I/O with 16-byte-aligned rows (what the module
-// passes), head dim HD in {32, 64, 128}: a thread owns 8 adjacent channels of
-// a run of TPT tokens plus the three rows before them (the conv window), so
+// passes), head dim HD in {32, 64, 128}: the tile's input rows (and the three
+// before it, the conv window) arrive in shared memory by 16-byte cp.async
+// copies, and a thread owns 8 adjacent channels of a run of TPT tokens, so
 // every global access is 16 bytes per thread -- the thread-per-channel kernel
 // above issues 2-byte accesses, 64 bytes per warp request, and the SM's limit
 // on outstanding requests caps it near 0.6 TB/s.  Tiles of TTV = 32 tokens
@@ -199,6 +200,17 @@ constexpr int TTV = 32;   // tokens per vectorised prologue CTA
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
+// 16-byte asynchronous copy global -> shared (L2 only); src_bytes = 0 fills zeros
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 template <typename TIO, typename TG, int HD>
 __global__ void __launch_bounds__(128)
 prologue_vec_kernel(const PrologueParams p) {
@@ -206,6 +218,7 @@ prologue_vec_kernel(const PrologueParams p) {
   static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
   __shared__ __align__(16) float ys[TTV][HD + 4];
   __shared__ float rstd[TTV];
+  __shared__ __align__(16) TIO xst[TTV + 3][HD];    // input rows t0 - 3 .. t0 + TTV - 1
   const int tid = threadIdx.x, cg = tid % CG, tg = tid / CG;
   const int lane = tid & 31, warp = tid >> 5;
   const int tensor = blockIdx.y / p.H, h = blockIdx.y - tensor * p.H;
@@ -257,19 +270,24 @@ prologue_vec_kernel(const PrologueParams p) {
   const float* bias = tensor == 0 ? p.b_q : tensor == 1 ? p.b_k : p.b_v;
   const int cs = p.conv_size, keep = cs - 1;
 
-  // rows t0 + i0 - 3 .. t0 + i0 + TPT - 1, every load issued before any use
-  float xv[TPT + 3][8];
-#pragma unroll
-  for (int r = 0; r < TPT + 3; ++r) {
-    const int i = i0 - 3 + r, t = t0 + i;
+  // the tile's rows t0 - 3 .. t0 + TTV - 1 of this head into shared memory by
+  // 16-byte asynchronous copies (no registers held while they fly; rows
+  // outside the input and the history are zero-filled)
+  const TIO* xh = x - 8 * cg;                      // channel 0 of this head
+  const TIO* hh = hb ? hb - 8 * cg : nullptr;
+  for (int q = tid; q < (TTV + 3) * CG; q += 128) {
+    const int row = q / CG, c8 = q - row * CG;
+    const int i = row - 3, t = t0 + i;
+    const TIO* src = xh;
+    uint32_t bytes = 0;
     if (i < nt && t >= 0) {
-      ld8v(x + (int64_t)t * xs, xv[r]);
-    } else if (i < nt && hb != nullptr && t >= -keep) {
-      ld8v(hb + (int64_t)(keep + t) * D, xv[r]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) xv[r][e] = 0.f;
+      src = xh + (int64_t)t * xs + 8 * c8;
+      bytes = 16;
+    } else if (i < nt && hh != nullptr && t >= -keep) {
+      src = hh + (int64_t)(keep + t) * D + 8 * c8;
+      bytes = 16;
     }
+    cp_async16(&xst[row][8 * c8], src, bytes);
   }
   // taps at the right end of a four-wide window, as in the kernel above
   float wv[8][4], bv[8];
@@ -279,16 +297,21 @@ prologue_vec_kernel(const PrologueParams p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) wv[e][j] = (j >= 4 - cs) ? w[e * cs + j - (4 - cs)] : 0.f;
   }
+  cp_async_wait_all();
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < TPT; ++i) {
     if (i0 + i >= nt) break;
+    float xw[4][8];                                // rows t - 3 .. t of the window
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ld8v(&xst[i0 + i + j][8 * cg], xw[j]);
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float acc = bv[e];
 #pragma unroll
       for (int j = 0; j < 4; ++j)
-        if (j >= 4 - cs) acc = fmaf(xv[i + j][e], wv[e][j], acc);
+        if (j >= 4 - cs) acc = fmaf(xw[j][e], wv[e][j], acc);
       y[e] = rnd<TIO>(silu_fast(rnd<TIO>(acc)));
     }
     *reinterpret_cast<float4*>(&ys[i0 + i][8 * cg]) = make_float4(y[0], y[1], y[2], y[3]);

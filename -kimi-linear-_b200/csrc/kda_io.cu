@@ -187,16 +187,18 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 }
 
 // The same prologue for 16-bit I/O with 16-byte-aligned rows (what the module
-// passes), head dim HD in {32, 64, 128}: the tile's input rows (and the three
-// before it, the conv window) arrive in shared memory by 16-byte cp.async
-// copies, and a thread owns 8 adjacent channels of a run of TPT tokens, so
+// passes), head dim HD in {32, 64, 128}: a CTA walks NTL tiles; a tile's input
+// rows (and the three before it, the conv window) arrive in one of two
+// shared-memory buffers by 16-byte cp.async copies issued while the previous
+// tile computes, and a thread owns 8 adjacent channels of a run of TPT tokens, so
 // every global access is 16 bytes per thread -- the thread-per-channel kernel
 // above issues 2-byte accesses, 64 bytes per warp request, and the SM's limit
 // on outstanding requests caps it near 0.6 TB/s.  Tiles of TTV = 32 tokens
 // (fewer registers per thread, more CTAs per SM).  Same rounding points; SiLU
 // uses the fast exponential and divide, whose ~1e-6 relative error vanishes
 // in the rounding of its output to the 16-bit I/O type.
-constexpr int TTV = 32;   // tokens per vectorised prologue CTA
+constexpr int TTV = 32;   // tokens per tile of the vectorised prologue
+constexpr int NTL = 4;    // tiles per CTA: the next tile's copies fly while this one computes
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
@@ -207,8 +209,12 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
                "l"(src), "r"(src_bytes)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// every committed group of this thread except the newest one has landed
+__device__ __forceinline__ void cp_async_wait_prev() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
 }
 
 template <typename TIO, typename TG, int HD>
@@ -218,14 +224,14 @@ prologue_vec_kernel(const PrologueParams p) {
   static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
   __shared__ __align__(16) float ys[TTV][HD + 4];
   __shared__ float rstd[TTV];
-  __shared__ __align__(16) TIO xst[TTV + 3][HD];    // input rows t0 - 3 .. t0 + TTV - 1
+  __shared__ __align__(16) TIO xst[2][TTV + 3][HD];   // input rows t0 - 3 .. t0 + TTV - 1
   const int tid = threadIdx.x, cg = tid % CG, tg = tid / CG;
   const int lane = tid & 31, warp = tid >> 5;
   const int tensor = blockIdx.y / p.H, h = blockIdx.y - tensor * p.H;
   const int b = blockIdx.z;
-  const int t0 = blockIdx.x * TTV;
-  const int nt = min(TTV, p.T - t0);
-  const int i0 = tg * TPT;                         // first token of this thread in the tile
+  const int tile0 = blockIdx.x * NTL;
+  const int ntl = min(NTL, (p.T + TTV - 1) / TTV - tile0);
+  const int i0 = tg * TPT;                         // first token of this thread in a tile
 
   if (tensor == 3) {                               // decay and beta gates
     const int ch0 = h * p.K + 8 * cg;
@@ -237,6 +243,9 @@ prologue_vec_kernel(const PrologueParams p) {
     }
     const TG* gk = static_cast<const TG*>(p.gk) + b * p.gk_s[0] + ch0;
     float* g = p.g + b * p.g_s[0] + h * p.g_s[2] + 8 * cg;
+    for (int k = 0; k < ntl; ++k) {
+    const int t0 = (tile0 + k) * TTV;
+    const int nt = min(TTV, p.T - t0);
     float gv[TPT][8];
 #pragma unroll
     for (int i = 0; i < TPT; ++i)
@@ -256,6 +265,7 @@ prologue_vec_kernel(const PrologueParams p) {
       const TG* bl = static_cast<const TG*>(p.beta_logit) + b * p.bl_s[0] + (int64_t)t * p.bl_s[1] + h;
       p.beta[b * p.beta_s[0] + (int64_t)t * p.beta_s[1] + h] = sigmoidf(ld(bl));
     }
+    }  // tiles
     return;
   }
 
@@ -270,25 +280,30 @@ prologue_vec_kernel(const PrologueParams p) {
   const float* bias = tensor == 0 ? p.b_q : tensor == 1 ? p.b_k : p.b_v;
   const int cs = p.conv_size, keep = cs - 1;
 
-  // the tile's rows t0 - 3 .. t0 + TTV - 1 of this head into shared memory by
-  // 16-byte asynchronous copies (no registers held while they fly; rows
-  // outside the input and the history are zero-filled)
+  // tile k's rows t0 - 3 .. t0 + TTV - 1 of this head into staging buffer
+  // k % 2 by 16-byte asynchronous copies (no registers held while they fly;
+  // rows outside the input and the history are zero-filled)
   const TIO* xh = x - 8 * cg;                      // channel 0 of this head
   const TIO* hh = hb ? hb - 8 * cg : nullptr;
-  for (int q = tid; q < (TTV + 3) * CG; q += 128) {
-    const int row = q / CG, c8 = q - row * CG;
-    const int i = row - 3, t = t0 + i;
-    const TIO* src = xh;
-    uint32_t bytes = 0;
-    if (i < nt && t >= 0) {
-      src = xh + (int64_t)t * xs + 8 * c8;
-      bytes = 16;
-    } else if (i < nt && hh != nullptr && t >= -keep) {
-      src = hh + (int64_t)(keep + t) * D + 8 * c8;
-      bytes = 16;
+  auto stage = [&](int k) {
+    const int t0 = (tile0 + k) * TTV, nt = min(TTV, p.T - t0);
+    for (int q = tid; q < (TTV + 3) * CG; q += 128) {
+      const int row = q / CG, c8 = q - row * CG;
+      const int i = row - 3, t = t0 + i;
+      const TIO* src = xh;
+      uint32_t bytes = 0;
+      if (i < nt && t >= 0) {
+        src = xh + (int64_t)t * xs + 8 * c8;
+        bytes = 16;
+      } else if (i < nt && hh != nullptr && t >= -keep) {
+        src = hh + (int64_t)(keep + t) * D + 8 * c8;
+        bytes = 16;
+      }
+      cp_async16(&xst[k & 1][row][8 * c8], src, bytes);
     }
-    cp_async16(&xst[row][8 * c8], src, bytes);
-  }
+  };
+  stage(0);
+  cp_async_commit();
   // taps at the right end of a four-wide window, as in the kernel above
   float wv[8][4], bv[8];
 #pragma unroll
@@ -297,14 +312,23 @@ prologue_vec_kernel(const PrologueParams p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) wv[e][j] = (j >= 4 - cs) ? w[e * cs + j - (4 - cs)] : 0.f;
   }
-  cp_async_wait_all();
+  const bool norm = tensor < 2;
+  TIO* out = static_cast<TIO*>(tensor == 0 ? p.q : tensor == 1 ? p.k : p.v) +
+             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + 8 * cg;
+  const int64_t os = p.out_s[tensor][1];
+  for (int k = 0; k < ntl; ++k) {
+  const int t0 = (tile0 + k) * TTV;
+  const int nt = min(TTV, p.T - t0);
+  if (k + 1 < ntl) stage(k + 1);                   // into the buffer tile k - 1 used
+  cp_async_commit();                               // (empty on the last tile)
+  cp_async_wait_prev();                            // tile k's copies have landed
   __syncthreads();
 #pragma unroll
   for (int i = 0; i < TPT; ++i) {
     if (i0 + i >= nt) break;
     float xw[4][8];                                // rows t - 3 .. t of the window
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ld8v(&xst[i0 + i + j][8 * cg], xw[j]);
+    for (int j = 0; j < 4; ++j) ld8v(&xst[k & 1][i0 + i + j][8 * cg], xw[j]);
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -333,7 +357,6 @@ prologue_vec_kernel(const PrologueParams p) {
   }
   __syncthreads();
 
-  const bool norm = tensor < 2;
   if (norm) {                                      // per-token L2 norm over the head
     for (int i = warp; i < nt; i += 4) {
       float ss = 0.f;
@@ -344,9 +367,6 @@ prologue_vec_kernel(const PrologueParams p) {
     }
     __syncthreads();
   }
-  TIO* out = static_cast<TIO*>(tensor == 0 ? p.q : tensor == 1 ? p.k : p.v) +
-             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + 8 * cg;
-  const int64_t os = p.out_s[tensor][1];
 #pragma unroll
   for (int i = 0; i < TPT; ++i) {
     if (i0 + i >= nt) break;
@@ -356,6 +376,8 @@ prologue_vec_kernel(const PrologueParams p) {
     for (int e = 0; e < 8; ++e) y[e] = norm ? ys[i0 + i][8 * cg + e] * r : ys[i0 + i][8 * cg + e];
     st8v(out + (int64_t)(t0 + i0 + i) * os, y);
   }
+  __syncthreads();                                 // ys, rstd and this staging buffer free
+  }  // tiles
 }
 
 // one warp per (b, t, h) row of V channels (V <= 128, multiple of 32)
@@ -418,7 +440,7 @@ static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
   dim3 grid((p.T + TT - 1) / TT, 4 * p.H, p.B);
   if constexpr (!std::is_same<TIO, float>::value) {
     if (vec_ok(p, sizeof(TG))) {
-      const dim3 vgrid((p.T + TTV - 1) / TTV, 4 * p.H, p.B);
+      const dim3 vgrid((p.T + TTV * NTL - 1) / (TTV * NTL), 4 * p.H, p.B);
       switch (p.K) {
         case 32: prologue_vec_kernel<TIO, TG, 32><<<vgrid, 128, 0, s>>>(p); break;
         case 64: prologue_vec_kernel<TIO, TG, 64><<<vgrid, 128, 0, s>>>(p); break;

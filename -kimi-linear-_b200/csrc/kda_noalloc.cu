@@ -15,7 +15,10 @@
 // is only a stand-in symbol), so the first call on each device looks up the
 // array's device address with cudaGetSymbolAddress while that device is
 // current and caches it; that first call should therefore happen before any
-// CUDA-graph stream capture begins.
+// CUDA-graph stream capture begins.  The cached address belongs to the
+// device's primary context (the one the CUDA runtime and PyTorch use); a
+// driver-API caller that makes its own context on the device must not call
+// this entry point from that context.
 //
 // All calls share the one array and each call overwrites it: the kernels write
 // every byte they later read, so nothing needs clearing, but two calls whose
@@ -45,8 +48,12 @@ int scratch_address(void** out) {
   std::lock_guard<std::mutex> lk(g_scratch_mu);
   if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      // clear the runtime's last-error slot: the next, unrelated call ends
+      // with cudaGetLastError and would otherwise report this failure again
+      (void)cudaGetLastError();
       return KDA_ERR_CUDA;
+    }
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];

@@ -25,7 +25,8 @@ Reported, all on the device with CUDA events on the launching stream:
 * ``mla_decode`` the MLA layer's static-buffer decode step of BASELINE
                 configs[4] (B=4, buffer 8192 + 256 latents), CUDA graph,
                 against HBM bandwidth (the rest of configs[4], the model
-                around it, cannot run on the GPU box: see DESIGN.md);
+                around it, cannot run on the GPU box: the reference's model code
+                does not travel with this repository);
 * ``fused_io``  the fused prologue / epilogue kernels of a KDA layer at the
                 configs[1] shape, against HBM bandwidth;
 * ``long_context`` BASELINE configs[3]: B=8, T=32768 bf16 prefill with a

@@ -120,8 +120,9 @@ int kda_recurrent_fwd(const KdaArgs* args, void* stream);
  * state_out.  Returns KDA_ERR_WORKSPACE when kda_chunkwise_workspace_bytes()
  * exceeds 32 MiB (B * H * ceil(T / 64) > 407 on the tensor-core path).  The
  * first call on a device looks up the array's address (cudaGetSymbolAddress),
- * so make it before any CUDA-graph capture; every GPU that loads the library
- * holds the array until exit.  All calls share the array: calls whose kernels
+ * so make it before any CUDA-graph capture; the address is cached per device
+ * for the primary context (the runtime's and PyTorch's).  Every GPU that
+ * loads the library holds the array until exit.  All calls share the array: calls whose kernels
  * overlap on the GPU race.  No counterpart in the reference.
  */
 int kda_chunkwise_fwd_noalloc(const KdaArgs* args, void* stream);

@@ -61,9 +61,18 @@ def test_noalloc_entry_point_matches_allocating_one(cuda_dev):
 
 
 def test_noalloc_refuses_problems_beyond_its_scratch(cuda_dev):
+    """The scratch holds 407 chunk images of 64 rows (82,432 bytes each): one
+    head of 407 x 64 tokens runs, one of 408 x 64 tokens is refused."""
     kb = pkg()
-    # 16 heads x 2,048 chunks of 64 rows would need about 2 GiB of scratch
-    x = kb.synth.make_inputs(1, 131072, 16, 128, 128, dtype=torch.float16, seed=22,
-                             device=cuda_dev)
-    st, _, _ = _noalloc_call(kb, x, cuda_dev)
-    assert st == kb._lib.KDA_ERR_WORKSPACE
+    for n_chunks, ok in ((407, True), (408, False)):
+        x = kb.synth.make_inputs(1, 64 * n_chunks, 1, 128, 128, dtype=torch.float16,
+                                 seed=22, device=cuda_dev)
+        st, o, S = _noalloc_call(kb, x, cuda_dev)
+        if ok:
+            assert st == 0, kb._lib.status_string(st)
+            o_ref, S_ref = kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"],
+                                            state_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert _rel(o, o_ref) < 2e-3 and _rel(S, S_ref) < 2e-3
+        else:
+            assert st == kb._lib.KDA_ERR_WORKSPACE

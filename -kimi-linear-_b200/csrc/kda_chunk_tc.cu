@@ -279,11 +279,13 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   const int total = NT * BH;                          // < 2^31 (checked on the host)
   const int stride = gridDim.x;
   int chunk = blockIdx.x;
-  // image whose ready flag thread 0 still owes (set once its bulk stores completed)
+  // image whose ready flag thread 0 still owes (set once its bulk stores
+  // completed; with `newest` the most recently committed store may still run)
   long pend = -1;
-  auto publish = [&]() {
+  auto publish = [&](bool newest) {
     if (pend >= 0) {
-      ptx::bulk_wait_all();
+      if (newest) ptx::bulk_wait_le<1>();
+      else ptx::bulk_wait_all();
       ptx::fence_proxy_async_global();
       __threadfence();
       ptx::st_release_gpu(flags + pend, 1u);
@@ -461,9 +463,9 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     A0[k0 + 1] = expf(gr[0].y);
   }
   if (tid < CH) sbeta[tid] = beta_c;
-  // the previous chunk's image is complete once its bulk stores are: publish
-  // it, which also frees the image staging region written from here on
-  if (tid == 0) publish();
+  // the image staging region is written from here on: the previous chunk's
+  // bulk stores must have read it
+  if (tid == 0) ptx::bulk_wait_read();
   __syncthreads();
   {
     float Zx[4], Zy[4], eZx[4], eZy[4];
@@ -667,6 +669,9 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     }
     }
   }
+  // the previous chunk's U^T / F^T store has had phases 1-2 to complete:
+  // publish that image (this chunk's Kbar^T / d store, the newest, may run on)
+  if (tid == 0) publish(true);
   __syncthreads();
 
   // ---- 3. M = (I + L)^-1 Diag(beta): blocked forward substitution ----------
@@ -859,11 +864,14 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     ptx::bulk_s2g(ws + img_off + IMG_U, img + IMG_U, IMG_BYTES - IMG_U);
     ptx::bulk_commit();
     pend = (long)(img_off / IMG_BYTES);
+    // a CTA's first chunk is published right away: the state pass starts on
+    // it (later chunks are published during the next chunk, off its path)
+    if (it == 0) publish(false);
   }
   ptx::tc_fence_after();
   }  // chunk loop
 
-  if (tid == 0) publish();
+  if (tid == 0) publish(false);
   if (warp == 0) {
     ptx::tmem_dealloc(*tslot, kPrepTmemCols);
   }
@@ -1162,16 +1170,19 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
       if (warp == 0) {                             // D3 = P16^T Kbar, then D2 = S16^T E^T
         ptx::tc_fence_after();
-        // E of chunk n landed, and the output warps read D2 of chunk n - 2 out
-        bool ok = mbar_wait_or_abort(&ofull[os], (n >> 1) & 1, abort_flag);
-        if (n >= 2) ok = ok && mbar_wait_or_abort(&d2free[os], ((n >> 1) - 1) & 1, abort_flag);
-        ptx::tc_fence_after();
         if (ptx::elect_one()) {
           const uint64_t bk = ptx::sdesc(sm0 + cs * CS_BYTES + CS_A3, 128, 1024);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             ptx::mma_f16_ts(tbase + TC_D3, tbase + TC_AP + 8 * ks, bk + 16 * ks, ID128, ks > 0);
           ptx::tc_commit(bd3);
+        }
+        __syncwarp();
+        // E of chunk n landed, and the output warps read D2 of chunk n - 2 out
+        bool ok = mbar_wait_or_abort(&ofull[os], (n >> 1) & 1, abort_flag);
+        if (n >= 2) ok = ok && mbar_wait_or_abort(&d2free[os], ((n >> 1) - 1) & 1, abort_flag);
+        ptx::tc_fence_after();
+        if (ptx::elect_one()) {
           if (ok) {
             const uint64_t be = ptx::sdesc(sm0 + ST_OS0 + os * OS_BYTES + OS_E, 128, 2048);
             const uint32_t d2 = tbase + (os ? TC_D2B : TC_D2A);

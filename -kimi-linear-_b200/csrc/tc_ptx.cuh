@@ -148,6 +148,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// wait until every committed bulk store except the newest N has completed
+template <int N>
+__device__ __forceinline__ void bulk_wait_le() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
 // flag publication between CTAs of concurrently running grids
 __device__ __forceinline__ void st_release_gpu(unsigned int* p, unsigned int v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

@@ -1120,22 +1120,28 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       for (int j = 0; j < 64; ++j) S[j] = 0.f;
     }
     bool bad = false, failed = false;
+    // f16 copy of S^T (A operand of D1, D2) into TMEM buffer `col`, 16 keys at a time
+    auto store_s16 = [&](uint32_t col, int q) {
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pk[i] = pack_h2(S[16 * q + 2 * i], S[16 * q + 2 * i + 1]);
+      asm volatile(
+          "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+              tl + col + 32 * hh + 8 * q),
+          "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]),
+          "r"(pk[7])
+          : "memory");
+    };
+#pragma unroll
+    for (int q = 0; q < 4; ++q) store_s16(TC_AS, q);
+    ptx::tmem_wait_st();
 #pragma unroll 1
     for (int n = 0; n < NT; ++n) {
       const int cs = n % ST_NCS, os = n & 1;
       const uint8_t* cst = sm + cs * CS_BYTES;
       const uint32_t as_col = TC_AS + 64 * (n & 1);
-      // (a) f16 copy of S^T -> TMEM; the buffer was last read by D1 / D2 of
-      // chunk n - 2, and D2 (the later of the two) must have completed
-      if (n >= 2) bad |= !mbar_wait_or_abort(&bd2[os], ((n >> 1) - 1) & 1, abort_flag);
-      ptx::tc_fence_after();
-      {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack_h2(S[2 * i], S[2 * i + 1]);
-        ptx::tmem_st<32>(tl + as_col + 32 * hh, reinterpret_cast<const float*>(pk));
-        ptx::tmem_wait_st();
-      }
+      // (a) the f16 copy of S^T(n) is in TMEM (written with the previous
+      // chunk's state update); image n's chain part must have landed
       ptx::tc_fence_before();
       bad |= !mbar_wait_or_abort(&cfull[cs], (n / ST_NCS) & 1, abort_flag);
       if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
@@ -1150,16 +1156,21 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
         }
         __syncwarp();
       }
-      // (b) P^T = U^T + D1 -> f16 -> TMEM
+      // (b) P^T = U^T + D1 -> f16 -> TMEM; U^T is read while D1 runs
+      int4 ur[4];
+      {
+        const uint8_t* urow = cst + CS_U + v * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ur[i] = *trow_chunk(urow, 4 * hh + i, v);
+      }
       bad |= !mbar_wait_or_abort(bd1, n & 1, abort_flag);
       ptx::tc_fence_after();
       {
         float x[32];
         ptx::tmem_ld<32>(tl + TC_D1 + 32 * hh, x);
         ptx::tmem_wait_ld();
-        const uint8_t* urow = cst + CS_U + v * 128;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) add8_f16(x + 8 * i, *trow_chunk(urow, 4 * hh + i, v));
+        for (int i = 0; i < 4; ++i) add8_f16(x + 8 * i, ur[i]);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = pack_h2(x[2 * i], x[2 * i + 1]);
@@ -1195,19 +1206,28 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
         __syncwarp();
         bad |= !ok;
       }
-      // (c) S^T <- S^T Diag(d) + D3; the chain part of this chunk is then consumed
+      // (c) S^T <- S^T Diag(d) + D3, and its f16 copy for chunk n + 1 into the
+      // other TMEM buffer, last read by D1 / D2 of chunk n - 1 (D2 the later)
       const float* dk = reinterpret_cast<const float*>(cst + CS_D) + 64 * hh;
+      if (n >= 1) bad |= !mbar_wait_or_abort(&bd2[os ^ 1], ((n - 1) >> 1) & 1, abort_flag);
       bad |= !mbar_wait_or_abort(bd3, n & 1, abort_flag);
       ptx::tc_fence_after();
+      const uint32_t as_next = TC_AS + 64 * ((n + 1) & 1);
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        float x[32];
-        ptx::tmem_ld<32>(tl + TC_D3 + 64 * hh + 32 * q, x);
+      for (int q = 0; q < 4; ++q) {
+        float dq[16], x[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 t = reinterpret_cast<const float4*>(dk + 16 * q)[i];
+          dq[4 * i] = t.x; dq[4 * i + 1] = t.y; dq[4 * i + 2] = t.z; dq[4 * i + 3] = t.w;
+        }
+        ptx::tmem_ld16(tl + TC_D3 + 64 * hh + 16 * q, x);
         ptx::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) S[32 * q + j] = fmaf(S[32 * q + j], dk[32 * q + j], x[j]);
+        for (int j = 0; j < 16; ++j) S[16 * q + j] = fmaf(S[16 * q + j], dq[j], x[j]);
+        store_s16(as_next, q);
       }
-      ptx::tc_fence_before();
+      ptx::tmem_wait_st();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&cempty[cs]);
     }

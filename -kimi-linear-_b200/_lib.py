@@ -14,7 +14,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libkda_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 FLAG_FORCE_SIMT = 1
@@ -163,6 +163,10 @@ class KdaBackwardArgs(ctypes.Structure):
         ("dstate_in", ctypes.c_void_p), ("dstate_in_stride", _I64x4),
         ("ckpt", ctypes.c_void_p),
         ("ckpt_floats", ctypes.c_size_t),
+        ("dq", ctypes.c_void_p), ("dq_stride", _I64x4),
+        ("dk", ctypes.c_void_p), ("dk_stride", _I64x4),
+        ("dg", ctypes.c_void_p), ("dg_stride", _I64x4),
+        ("dbeta", ctypes.c_void_p), ("dbeta_stride", _I64x3),
     ]
 
 

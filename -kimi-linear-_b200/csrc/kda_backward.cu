@@ -412,6 +412,69 @@ size_t backward_ckpt_floats(int B, int H, int T, int K, int V) {
   return (size_t)B * H * ((T + bwd::CK - 1) / bwd::CK) * K * V;
 }
 
+namespace bwd {
+// dq, dk (io dtype), dg, dbeta (fp32) = sums over the V/16 column tiles of the
+// partials [vt][b][t][h][k] and [vt][b][t][h]; a thread sums four consecutive
+// k of one (b, t, h) in tile order (deterministic), and (k4 == 0) its dbeta
+template <typename TIO>
+__global__ void __launch_bounds__(256)
+reduce_kernel(const BwdParams p) {
+  const int K4 = p.K >> 2, nvt = p.V >> 4;
+  const size_t rows = (size_t)p.B * p.T * p.H;
+  const size_t n = rows * p.K;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * K4;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / K4;
+    const int k = (int)(i - row * K4) * 4;
+    const int h = (int)(row % p.H);
+    const size_t bt = row / p.H;
+    const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+    float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4, g4 = q4;
+    float db = 0.f;
+    for (int vt = 0; vt < nvt; ++vt) {
+      const size_t o = vt * n + row * p.K + k;
+      const float4 a = *reinterpret_cast<const float4*>(p.dq_part + o);
+      const float4 c = *reinterpret_cast<const float4*>(p.dk_part + o);
+      const float4 e = *reinterpret_cast<const float4*>(p.dg_part + o);
+      q4.x += a.x; q4.y += a.y; q4.z += a.z; q4.w += a.w;
+      k4.x += c.x; k4.y += c.y; k4.z += c.z; k4.w += c.w;
+      g4.x += e.x; g4.y += e.y; g4.z += e.z; g4.w += e.w;
+      if (k == 0) db += p.dbeta_part[vt * rows + row];
+    }
+    const float qv[4] = {q4.x, q4.y, q4.z, q4.w}, kv[4] = {k4.x, k4.y, k4.z, k4.w};
+    TIO* dq = static_cast<TIO*>(p.dq) + b * p.dq_s[0] + (int64_t)t * p.dq_s[1] + h * p.dq_s[2] + k;
+    TIO* dk = static_cast<TIO*>(p.dk) + b * p.dk_s[0] + (int64_t)t * p.dk_s[1] + h * p.dk_s[2] + k;
+    float* dg = p.dg + b * p.dg_s[0] + (int64_t)t * p.dg_s[1] + h * p.dg_s[2] + k;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      st(dq + j, qv[j]);
+      st(dk + j, kv[j]);
+    }
+    dg[0] = g4.x; dg[1] = g4.y; dg[2] = g4.z; dg[3] = g4.w;
+    if (k == 0) p.dbeta[b * p.dbeta_s[0] + (int64_t)t * p.dbeta_s[1] + h * p.dbeta_s[2]] = db;
+  }
+}
+
+template <typename TIO>
+cudaError_t launch_reduce(const BwdParams& p, cudaStream_t s) {
+  const size_t work = (size_t)p.B * p.T * p.H * (p.K >> 2);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t want = (work + 255) / 256, cap = (size_t)sms * 8;
+  reduce_kernel<TIO><<<(unsigned)(want < cap ? want : cap), 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+}  // namespace bwd
+
+cudaError_t launch_backward_reduce(const BwdParams& p, cudaStream_t s) {
+  switch (p.io_dtype) {
+    case KDA_DTYPE_F32: return bwd::launch_reduce<float>(p, s);
+    case KDA_DTYPE_F16: return bwd::launch_reduce<__half>(p, s);
+    default: return bwd::launch_reduce<__nv_bfloat16>(p, s);
+  }
+}
+
 cudaError_t launch_backward(const BwdParams& p, cudaStream_t s) {
   switch (p.io_dtype) {
     case KDA_DTYPE_F32: return bwd::launch_si<float>(p, s);

@@ -256,6 +256,11 @@ int validate_backward(const KdaBackwardArgs* a) {
   if (a->dstate_in != nullptr && a->dstate_in_stride[3] != 1) return KDA_ERR_STRIDE;
   if (a->ckpt_floats < backward_ckpt_floats(a->B, a->H, a->T, a->K, a->V)) return KDA_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(a->ckpt) % 16) return KDA_ERR_ALIGNMENT;
+  if (a->dq != nullptr) {
+    if (!a->dk || !a->dg || !a->dbeta) return KDA_ERR_NULL_POINTER;
+    if (a->dq_stride[3] != 1 || a->dk_stride[3] != 1 || a->dg_stride[3] != 1)
+      return KDA_ERR_STRIDE;
+  }
   return KDA_OK;
 }
 
@@ -278,6 +283,10 @@ BwdParams to_backward(const KdaBackwardArgs* a) {
   p.dv = a->dv; std::memcpy(p.dv_s, a->dv_stride, sizeof(p.dv_s));
   p.dstate_in = a->dstate_in; std::memcpy(p.dsi_s, a->dstate_in_stride, sizeof(p.dsi_s));
   p.ckpt = a->ckpt;
+  p.dq = a->dq; std::memcpy(p.dq_s, a->dq_stride, sizeof(p.dq_s));
+  p.dk = a->dk; std::memcpy(p.dk_s, a->dk_stride, sizeof(p.dk_s));
+  p.dg = a->dg; std::memcpy(p.dg_s, a->dg_stride, sizeof(p.dg_s));
+  p.dbeta = a->dbeta; std::memcpy(p.dbeta_s, a->dbeta_stride, sizeof(p.dbeta_s));
   return p;
 }
 
@@ -387,7 +396,11 @@ int kda_backward(const KdaBackwardArgs* args, void* stream) {
   if (args->B == 0 || args->H == 0 || args->T == 0) return KDA_OK;
   st = check_arch();
   if (st != KDA_OK) return st;
-  return launch_status(launch_backward(to_backward(args), static_cast<cudaStream_t>(stream)));
+  const BwdParams p = to_backward(args);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = launch_backward(p, s);
+  if (e == cudaSuccess && p.dq != nullptr) e = launch_backward_reduce(p, s);
+  return launch_status(e);
 }
 
 size_t kda_backward_ckpt_floats(int B, int H, int T, int K, int V) {

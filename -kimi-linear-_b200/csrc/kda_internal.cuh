@@ -117,10 +117,17 @@ struct BwdParams {
   float* dv; int64_t dv_s[4];
   float* dstate_in; int64_t dsi_s[4];
   float* ckpt;
+  // optional final sums of the partials (dq == nullptr: partials only)
+  void* dq; int64_t dq_s[4];
+  void* dk; int64_t dk_s[4];
+  float* dg; int64_t dg_s[4];
+  float* dbeta; int64_t dbeta_s[3];
 };
 
 size_t backward_ckpt_floats(int B, int H, int T, int K, int V);
 cudaError_t launch_backward(const BwdParams& p, cudaStream_t s);
+// dq, dk, dg, dbeta = sums of the V/16 partials (after launch_backward)
+cudaError_t launch_backward_reduce(const BwdParams& p, cudaStream_t s);
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t s);
 cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s);

@@ -278,7 +278,8 @@ def kda_backward(q, k, v, g, beta, state, do, dS):
     None (zero initial state, ``dstate`` None) or [B, H, K, V] in any
     supported dtype.  dq, dk, dv come back in v's dtype, dg and dbeta fp32,
     dstate in ``state``'s dtype.  Reduction over V tiles: the kernel writes
-    per-16-column partial sums of dq, dk, dg and dbeta, summed here."""
+    per-16-column partial sums of dq, dk, dg and dbeta, which the library sums
+    into the final gradients in the same call."""
     fn = "kda_backward"
     dev = _check_tensors(fn, [("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
                               ("state", state), ("do", do), ("dS", dS)])
@@ -338,9 +339,17 @@ def kda_backward(q, k, v, g, beta, state, do, dS):
     a.dg_part, a.dbeta_part = dg_p.data_ptr(), db_p.data_ptr()
     a.dv, a.dv_stride = dv.data_ptr(), _strides(dv, 4)
     a.ckpt, a.ckpt_floats = ckpt.data_ptr(), ck_n
+    # the library sums the partials into the final gradients (same stream)
+    dq = torch.empty(B, T, H, K, device=dev, dtype=io)
+    dk = torch.empty_like(dq)
+    dg = torch.empty(B, T, H, K, device=dev, dtype=torch.float32)
+    db = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+    a.dq, a.dq_stride = dq.data_ptr(), _strides(dq, 4)
+    a.dk, a.dk_stride = dk.data_ptr(), _strides(dk, 4)
+    a.dg, a.dg_stride = dg.data_ptr(), _strides(dg, 4)
+    a.dbeta, a.dbeta_stride = db.data_ptr(), _strides(db, 3)
     _call(fn, lib.kda_backward, a, dev)
-    dq, dk, dg, db = dq_p.sum(0), dk_p.sum(0), dg_p.sum(0), db_p.sum(0)
-    return (dq.to(io), dk.to(io), dv.to(io), dg, db,
+    return (dq, dk, dv.to(io), dg, db,
             None if state is None else dstate.to(state.dtype))
 
 

@@ -227,6 +227,59 @@ def cpu_port_throughput(t_sample, heads, steps=1, warmup=0):
     return tokens / wall, wall
 
 
+def cpu_decode_throughput(steps=16):
+    """configs[2] on the host: ``oracle.kda_recurrent`` single-token steps on
+    the full fp32 state [64, 16, 128, 128] (numpy, one process), ``steps`` of
+    them timed and the per-step time extrapolated to the 1024-step workload.
+    Returns (tokens/s, s per step)."""
+    import numpy as np
+    from oracle import kda_oracle as O
+    rng = np.random.default_rng(2)
+    B, H, K, V = CFG2["B"], CFG2["H"], CFG2["K"], CFG2["V"]
+    S = (rng.standard_normal((B, H, K, V)) * 0.02).astype(np.float32)
+
+    def unit(shape):
+        x = rng.standard_normal(shape).astype(np.float32)
+        return (x / np.sqrt((x * x).sum(-1, keepdims=True))).astype(np.float16)
+    toks = []
+    for _ in range(steps):
+        a_log = np.log(rng.uniform(1, 16, (H, K))).astype(np.float32)
+        dt = np.log(np.expm1(rng.uniform(1e-3, 0.1, (H, K)))).astype(np.float32)
+        g = (-np.exp(a_log) * np.logaddexp(0, rng.standard_normal((B, 1, H, K)) + dt))
+        toks.append((unit((B, 1, H, K)), unit((B, 1, H, K)),
+                     rng.standard_normal((B, 1, H, V)).astype(np.float16), g.astype(np.float32),
+                     (1 / (1 + np.exp(-rng.standard_normal((B, 1, H))))).astype(np.float32)))
+    t0 = time.perf_counter()
+    for q, k, v, g, beta in toks:
+        _, S = O.kda_recurrent(q, k, v, g, beta, state=S, state_dtype="f32")
+    per = (time.perf_counter() - t0) / steps
+    return B / per, per
+
+
+def cpu_long_context_throughput(t_sample, heads):
+    """configs[3] on the host: ``oracle.kda_chunkwise`` on bf16-valued fp32
+    inputs (the fp32-transient arithmetic the reference intends for bf16,
+    ``kda.py:116``), S0 ~ N(0, 0.02), ``heads`` independent heads of
+    ``t_sample`` tokens in a spawn pool (one head per process).  A configs[3]
+    token is 16 heads, so the sample is ``t_sample * heads / 16`` tokens.
+    Returns (tokens/s, wall s)."""
+    import numpy as np
+    import torch
+    from oracle import kda_oracle as O
+    from oracle import pool as OP
+    kb = importlib.import_module("-kimi-linear-_b200")
+    x = kb.synth.make_inputs(1, t_sample, heads, 128, 128, dtype=torch.bfloat16, seed=5,
+                             s0_std=0.02)
+    f = lambda t: t.float().numpy()  # noqa: E731
+    t0 = time.perf_counter()
+    OP.chunkwise_by_head(f(x["q"]), f(x["k"]), f(x["v"]), x["g"].numpy(), x["beta"].numpy(),
+                         initial_state=x["S0"].numpy(), chunk_size=64, state_dtype="f32",
+                         v_dtype="bf16", procs=heads)
+    wall = time.perf_counter() - t0
+    del O, np
+    return t_sample * heads / 16 / wall, wall
+
+
 # --------------------------------------------------------------------------- #
 # GPU legs
 # --------------------------------------------------------------------------- #
@@ -635,6 +688,75 @@ def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
                          "unit": "GB/s", "algorithmic_bytes": byts}}
 
 
+def bench_backward(torch, kb, dev, steps, warmup, clk):
+    """configs[1] backward: the gradients of one ``kda_chunkwise`` call (B=1,
+    T=4096, H=16, fp16 q/k/v, fp32 state) for random output and final-state
+    gradients, through ``ops.kda_backward`` (checkpoint pass, reverse sweep and
+    the partial-sum reduction, all in the library).  Two rotating input sets.
+    Returns (ms per call, algorithmic bytes: every input read once and every
+    gradient written once)."""
+    B, T, H, K, V = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"], CFG1["V"]
+    gen = torch.Generator(device=dev).manual_seed(9)
+    sets = []
+    for s_ in range(2):
+        x = kb.synth.make_config(1, seed=20 + s_, device=dev)
+        x["do"] = torch.randn(B, T, H, V, generator=gen, device=dev).half()
+        x["dS"] = torch.randn(B, H, K, V, generator=gen, device=dev) * 0.01
+        sets.append(x)
+
+    def step(i):
+        x = sets[i % 2]
+        return kb.ops.kda_backward(x["q"], x["k"], x["v"], x["g"], x["beta"], None, x["do"],
+                                   x["dS"])
+
+    ms = _events_time(torch, step, steps, warmup, clk)
+    th = B * T * H
+    nbytes = th * (3 * K * 2 + K * 4 + 4 + V * 2) + B * H * K * V * 4 \
+        + th * (2 * K * 2 + V * 2 + K * 4 + 4)
+    return ms, nbytes
+
+
+def bench_cfg4_decode_layers(torch, kb, dev, steps, warmup, clk):
+    """The attention side of one configs[4] decode step at its layer shapes
+    (B=4, hidden 2048, 16 KDA heads x 128, conv 4, fp16): one KDA layer's core
+    work per token -- fused prologue (conv step from the cache, SiLU, L2 norm,
+    gates), the recurrent state update on the fp32 [4, 16, 128, 128] state
+    (in place, as GraphedDecoder keeps it) and the fused epilogue -- captured
+    in a CUDA graph on NBUF layer states and replayed.  The projections, FFN
+    and MLA/KDA output projections (cuBLAS GEMMs of the model) are not part of
+    it.  Returns ms per KDA layer per decode step."""
+    B, H, K, cs = 4, 16, 128, 4
+    D = H * K
+    NBUF = 8
+    g = torch.Generator(device=dev).manual_seed(13)
+    f16 = torch.float16
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(f16)
+    layers = []
+    for _ in range(NBUF):
+        layers.append(dict(
+            x=[rnd(B, 1, D) for _ in range(4)], beta=rnd(B, 1, H), og=rnd(B, 1, D),
+            hist={n: rnd(B, cs - 1, D) for n in "qkv"},
+            w=[(torch.randn(D, 1, cs, generator=g, device=dev) * 0.4).to(f16).float()
+               for _ in range(3)],
+            b=[(torch.randn(D, generator=g, device=dev) * 0.1).to(f16).float() for _ in range(3)],
+            A_log=torch.log(torch.rand(H, K, generator=g, device=dev) * 15 + 1),
+            dt=torch.log(torch.expm1(torch.rand(H, K, generator=g, device=dev) * 0.099 + 1e-3)),
+            S=torch.randn(B, H, K, K, generator=g, device=dev) * 0.02,
+            nw=torch.rand(H, K, generator=g, device=dev) + 0.5))
+
+    def layer(i):
+        L = layers[i % NBUF]
+        q, k, v, gg, beta, _ = kb.kda_prologue(*L["x"], L["beta"], L["w"], L["b"], L["A_log"],
+                                                L["dt"], H, K, K, 1e-6, conv_cache=L["hist"])
+        o, _ = kb.kda_recurrent(q, k, v, gg, beta, state=L["S"], state_dtype=torch.float32,
+                                inplace=True)
+        return kb.kda_epilogue(o, L["og"], L["nw"], 1e-6)
+
+    return _graph_time(torch, dev, layer, NBUF, steps, warmup, clk)
+
+
 def profile_case(which, reps=3):
     """Three calls of one workload on cuda:0 (the target of the ncu captures
     summarised under profiles/): ``prefill`` = configs[1], ``decode`` = one
@@ -684,6 +806,8 @@ def main():
                     help="timed steps of the configs[4] MLA decode leg")
     ap.add_argument("--io-steps", type=int, default=50,
                     help="timed calls of the fused prologue / epilogue leg (0 skips it)")
+    ap.add_argument("--bwd-steps", type=int, default=6,
+                    help="timed calls of the configs[1] backward leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=("prefill", "decode", "mla"),
                     help="profiling target: run the workload three times, print nothing timed")
@@ -701,7 +825,7 @@ def main():
         if rank != 0:
             return
         heads = max(1, min(os.cpu_count() or 1, 16))
-        t_sample = 1024
+        t_sample = CFG1["T"]        # the same sample as the cpu_baseline leg of the kda arm
         val, wall = cpu_port_throughput(t_sample, heads, steps=a.steps, warmup=a.warmup)
         line = {
             "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": a.gpus,
@@ -745,12 +869,16 @@ def main():
                                                         clk)
         io_ms = bench_fused_io(torch, kb, dev, a.io_steps, a.warmup, clk) \
             if a.io_steps > 0 else None
+        bwd = bench_backward(torch, kb, dev, a.bwd_steps, 2, clk) if a.bwd_steps > 0 else None
+        cfg4_layer_ms = bench_cfg4_decode_layers(torch, kb, dev, max(64, a.mla_steps), a.warmup,
+                                                 clk)
         long_ctx = None
         if a.long_steps > 0:
             long_ctx = bench_long_context(torch, kb, dev, a.long_steps, 3, dist, world,
                                           rank, clk)
     clocks = clk.summary()
-    # kernels per prefill call: prep + state pass on the tensor-core path
+    # kernels per prefill call: prep + state pass on the tensor-core path (the
+    # ready-flag reset before them is a memset node, not a kernel)
     launches_per_call = 2 if path == "tcgen05" else 1
 
     hbm, tc, peak_kind = _peaks()
@@ -763,15 +891,26 @@ def main():
                                          + 2 * CFG2["K"] * 2 + CFG2["V"] * 2 + CFG2["K"] * 4
                                          + 4 + CFG2["V"] * 2)
 
-    cpu = None
+    cpu = cpu_dec = cpu_long = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         heads = max(1, min(os.cpu_count() or 1, 16))
-        t_sample = 4096
-        val, wall = cpu_port_throughput(t_sample, heads, steps=2)
+        t_sample = CFG1["T"]
+        val, wall = cpu_port_throughput(t_sample, heads, steps=2, warmup=1)
         cpu = {"value": val, "unit": "tokens/s", "cores": heads, "kind": "port",
                "sample": f"{heads} heads x {t_sample} tokens of configs[1] "
                          f"({wall:.2f} s per step), numpy port of kda.py:58-185, fp32 "
                          f"transients on fp16-valued inputs"}
+        dval, dper = cpu_decode_throughput()
+        cpu_dec = {"value": dval, "unit": "tokens/s", "cores": 1, "kind": "port",
+                   "sample": f"16 single-token steps of configs[2] on the full fp32 state "
+                             f"[64,16,128,128] ({dper * 1e3:.1f} ms per step), numpy port of "
+                             f"kda.py:188-219, extrapolated to the 1024-step workload"}
+        lt = 8192
+        lval, lwall = cpu_long_context_throughput(lt, heads)
+        cpu_long = {"value": lval, "unit": "tokens/s", "cores": heads, "kind": "port",
+                    "sample": f"{heads} heads x {lt} tokens of configs[3] ({lwall:.2f} s), "
+                              f"numpy port of kda.py:58-185 on bf16-valued fp32 inputs "
+                              f"with S0 ~ N(0, 0.02)"}
 
     if rank == 0:
         ach = pre_bytes / (ms_step * 1e-3) / 1e9
@@ -812,8 +951,12 @@ def main():
                        "roofline": {"bound": "hbm", "achieved": dec_bytes / (dec_ms * 1e-3) / 1e9,
                                     "peak": hbm, "unit": "GB/s",
                                     "frac": dec_bytes / (dec_ms * 1e-3) / 1e9 / hbm,
-                                    "traffic": _traffic("kda_recurrent", "cfg2"),
-                                    "algorithmic_bytes": dec_bytes}},
+                                    "traffic": None,
+                                    "traffic_note": "a single-launch ncu capture leaves the "
+                                                    "state write in L2 and under-counts the "
+                                                    "steady state; not reported",
+                                    "algorithmic_bytes": dec_bytes},
+                       "cpu_baseline": cpu_dec},
             "mla_decode": {"workload": "MLA static-buffer decode step of configs[4] "
                                        "(B=4, 16 heads, kv_lora_rank 512, head dims 128, "
                                        "buffer 8192 + 256 latents, fp16)",
@@ -840,7 +983,28 @@ def main():
                                        "algorithmic_bytes": nb}}
                    for name, ms, nb in (("prologue", io_ms[0], io_ms[2]),
                                         ("epilogue", io_ms[1], io_ms[3]))}},
-            "long_context": long_ctx,
+            "long_context": None if long_ctx is None else {**long_ctx,
+                                                           "cpu_baseline": cpu_long},
+            "backward": None if bwd is None else {
+                "workload": "gradients of one kda_chunkwise call at configs[1] (B=1, T=4096, "
+                            "H=16, fp16, fp32 state) for random do and dS, ops.kda_backward "
+                            "(checkpoint pass, reverse sweep, partial-sum reduction)",
+                "value": tokens / (bwd[0] * 1e-3), "unit": "tokens/s",
+                "ms_per_call": bwd[0],
+                "roofline": {"bound": "hbm", "achieved": bwd[1] / (bwd[0] * 1e-3) / 1e9,
+                             "peak": hbm, "unit": "GB/s",
+                             "frac": bwd[1] / (bwd[0] * 1e-3) / 1e9 / hbm,
+                             "algorithmic_bytes": bwd[1],
+                             "note": "token-serial reverse sweep, instruction-bound"}},
+            "configs4_decode": {
+                "workload": "configs[4] decode step, attention side at its layer shapes "
+                            "(B=4, fp16): 18 KDA layers x (fused prologue + recurrent "
+                            "state update in place + fused epilogue) and 6 MLA static-buffer "
+                            "steps; the model's projection / FFN GEMMs are not included (the "
+                            "reference model code does not travel with this repository)",
+                "kda_layer_ms": cfg4_layer_ms, "mla_step_ms": mla_ms,
+                "attention_ms_per_decode_step": 18 * cfg4_layer_ms + 6 * mla_ms,
+                "kda_share": 18 * cfg4_layer_ms / (18 * cfg4_layer_ms + 6 * mla_ms)},
             "gpu_launches": a.steps * launches_per_call,
             "clocks": clocks,
             "cpu_baseline": cpu,

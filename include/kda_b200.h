@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define KDA_B200_ABI_VERSION 1
+#define KDA_B200_ABI_VERSION 2
 
 /* Element types. */
 typedef enum {
@@ -245,6 +245,9 @@ int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream);
  *                16-column tiles of V (dq, dk, dg = their sums over axis 0)
  *   dbeta_part : [V/16, B, T, H] fp32 partial sums
  *   ckpt       : workspace of kda_backward_ckpt_floats() fp32 values
+ *   dq, dk     : [B, T, H, K] in io_dtype, or NULL; when dq is set, the call
+ *                also sums the partials into dq, dk, dg ([B, T, H, K] fp32)
+ *                and dbeta ([B, T, H] fp32) on the same stream
  * Requires K in {32, 64, 128} and V % 16 == 0.
  */
 typedef struct KdaBackwardArgs {
@@ -269,6 +272,10 @@ typedef struct KdaBackwardArgs {
   float* dstate_in;  int64_t dstate_in_stride[4];
   float* ckpt;
   size_t ckpt_floats;
+  void* dq;          int64_t dq_stride[4];      /* NULL: partial sums only */
+  void* dk;          int64_t dk_stride[4];
+  float* dg;         int64_t dg_stride[4];
+  float* dbeta;      int64_t dbeta_stride[3];
 } KdaBackwardArgs;
 
 int kda_backward(const KdaBackwardArgs* args, void* stream);

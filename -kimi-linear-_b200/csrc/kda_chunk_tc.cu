@@ -1120,6 +1120,24 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       for (int j = 0; j < 64; ++j) S[j] = 0.f;
     }
     bool bad = false, failed = false;
+    // D2(j) = S16^T(j) E_j^T into D2 buffer j & 1 (warp 0): E_j landed, and the
+    // output warps read D2(j - 2) out of that buffer
+    auto issue_d2 = [&](int j) -> bool {
+      const int jb = j & 1;
+      bool ok = mbar_wait_or_abort(&ofull[jb], (j >> 1) & 1, abort_flag);
+      if (j >= 2) ok = ok && mbar_wait_or_abort(&d2free[jb], ((j >> 1) - 1) & 1, abort_flag);
+      ptx::tc_fence_after();
+      if (ok && ptx::elect_one()) {
+        const uint64_t be = ptx::sdesc(sm0 + ST_OS0 + jb * OS_BYTES + OS_E, 128, 2048);
+        const uint32_t d2 = tbase + (jb ? TC_D2B : TC_D2A);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          ptx::mma_f16_ts(d2, tbase + TC_AS + 64 * jb + 8 * ks, be + 16 * ks, ID64, ks > 0);
+        ptx::tc_commit(&bd2[jb]);
+      }
+      __syncwarp();
+      return ok;
+    };
     // f16 copy of S^T (A operand of D1, D2) into TMEM buffer `col`, 16 keys at a time
     auto store_s16 = [&](uint32_t col, int q) {
       uint32_t pk[8];
@@ -1145,7 +1163,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       ptx::tc_fence_before();
       bad |= !mbar_wait_or_abort(&cfull[cs], (n / ST_NCS) & 1, abort_flag);
       if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
-      if (warp == 0) {                             // D1 = S16^T (-W)^T
+      if (warp == 0) {                             // D1 = S16^T (-W)^T, then D2(n - 1)
         ptx::tc_fence_after();
         if (ptx::elect_one()) {
           const uint64_t bw = ptx::sdesc(sm0 + cs * CS_BYTES + CS_W, 128, 2048);
@@ -1155,6 +1173,10 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
           ptx::tc_commit(bd1);
         }
         __syncwarp();
+        // the previous chunk's output GEMM goes in behind D1, so the tensor
+        // pipe runs it during the P hand-off instead of between D3 and the
+        // next D1 (its waits are off the chain: D1 is already issued)
+        if (n >= 1) bad |= !issue_d2(n - 1);
       }
       // (b) P^T = U^T + D1 -> f16 -> TMEM; U^T is read while D1 runs
       int4 ur[4];
@@ -1179,7 +1201,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       }
       ptx::tc_fence_before();
       if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
-      if (warp == 0) {                             // D3 = P16^T Kbar, then D2 = S16^T E^T
+      if (warp == 0) {                             // D3 = P16^T Kbar
         ptx::tc_fence_after();
         if (ptx::elect_one()) {
           const uint64_t bk = ptx::sdesc(sm0 + cs * CS_BYTES + CS_A3, 128, 1024);
@@ -1189,22 +1211,6 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
           ptx::tc_commit(bd3);
         }
         __syncwarp();
-        // E of chunk n landed, and the output warps read D2 of chunk n - 2 out
-        bool ok = mbar_wait_or_abort(&ofull[os], (n >> 1) & 1, abort_flag);
-        if (n >= 2) ok = ok && mbar_wait_or_abort(&d2free[os], ((n >> 1) - 1) & 1, abort_flag);
-        ptx::tc_fence_after();
-        if (ptx::elect_one()) {
-          if (ok) {
-            const uint64_t be = ptx::sdesc(sm0 + ST_OS0 + os * OS_BYTES + OS_E, 128, 2048);
-            const uint32_t d2 = tbase + (os ? TC_D2B : TC_D2A);
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks)
-              ptx::mma_f16_ts(d2, tbase + as_col + 8 * ks, be + 16 * ks, ID64, ks > 0);
-            ptx::tc_commit(&bd2[os]);
-          }
-        }
-        __syncwarp();
-        bad |= !ok;
       }
       // (c) S^T <- S^T Diag(d) + D3, and its f16 copy for chunk n + 1 into the
       // other TMEM buffer, last read by D1 / D2 of chunk n - 1 (D2 the later)
@@ -1231,6 +1237,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&cempty[cs]);
     }
+    if (!failed && warp == 0) bad |= !issue_d2(NT - 1);     // the last chunk's output GEMM
     if (!failed) failed = ptx::bar_red_or(1, ST_CHAIN, bad);
     if (failed) {
       *abort_flag = 1;

@@ -222,8 +222,6 @@ __global__ void __launch_bounds__(128)
 prologue_vec_kernel(const PrologueParams p) {
   constexpr int CG = HD / 8, TGRP = 128 / CG, TPT = TTV / TGRP;
   static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
-  __shared__ __align__(16) float ys[TTV][HD + 4];
-  __shared__ float rstd[TTV];
   __shared__ __align__(16) TIO xst[2][TTV + 3][HD];   // input rows t0 - 3 .. t0 + TTV - 1
   const int tid = threadIdx.x, cg = tid % CG, tg = tid / CG;
   const int lane = tid & 31, warp = tid >> 5;
@@ -323,23 +321,41 @@ prologue_vec_kernel(const PrologueParams p) {
   cp_async_commit();                               // (empty on the last tile)
   cp_async_wait_prev();                            // tile k's copies have landed
   __syncthreads();
+  // the thread's TPT tokens need window rows i0 .. i0 + TPT + 2: each row is
+  // read from shared memory once and slides through the four-row window.  The
+  // CG channel groups of a token are CG consecutive lanes, so the per-token L2
+  // norm is a shuffle reduction (rows past nt are zeros and are not stored).
+  {
+    const TIO* xb = &xst[k & 1][i0][8 * cg];
+    float xw[4][8];
 #pragma unroll
-  for (int i = 0; i < TPT; ++i) {
-    if (i0 + i >= nt) break;
-    float xw[4][8];                                // rows t - 3 .. t of the window
+    for (int j = 0; j < 3; ++j) ld8v(xb + j * HD, xw[j + 1]);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ld8v(&xst[k & 1][i0 + i + j][8 * cg], xw[j]);
-    float y[8];
+    for (int i = 0; i < TPT; ++i) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float acc = bv[e];
+      for (int j = 0; j < 3; ++j)
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (j >= 4 - cs) acc = fmaf(xw[j][e], wv[e][j], acc);
-      y[e] = rnd<TIO>(silu_fast(rnd<TIO>(acc)));
+        for (int e = 0; e < 8; ++e) xw[j][e] = xw[j + 1][e];
+      ld8v(xb + (i + 3) * HD, xw[3]);
+      float y[8], ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float acc = bv[e];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j >= 4 - cs) acc = fmaf(xw[j][e], wv[e][j], acc);
+        y[e] = rnd<TIO>(silu_fast(rnd<TIO>(acc)));
+        ss = fmaf(y[e], y[e], ss);
+      }
+      if (norm) {
+#pragma unroll
+        for (int off = 1; off < CG; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float r = fminf(rsqrtf(ss), 1.f / p.eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] *= r;
+      }
+      if (i0 + i < nt) st8v(out + (int64_t)(t0 + i0 + i) * os, y);
     }
-    *reinterpret_cast<float4*>(&ys[i0 + i][8 * cg]) = make_float4(y[0], y[1], y[2], y[3]);
-    *reinterpret_cast<float4*>(&ys[i0 + i][8 * cg + 4]) = make_float4(y[4], y[5], y[6], y[7]);
   }
   // new conv cache: the last keep inputs of cat(history, x)
   if (p.new_q != nullptr && t0 + nt == p.T && keep > 0 && tg == 0) {
@@ -355,28 +371,7 @@ prologue_vec_kernel(const PrologueParams p) {
       }
     }
   }
-  __syncthreads();
-
-  if (norm) {                                      // per-token L2 norm over the head
-    for (int i = warp; i < nt; i += 4) {
-      float ss = 0.f;
-      for (int cc = lane; cc < HD; cc += 32) ss = fmaf(ys[i][cc], ys[i][cc], ss);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (lane == 0) rstd[i] = fminf(rsqrtf(ss), 1.f / p.eps);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < TPT; ++i) {
-    if (i0 + i >= nt) break;
-    float y[8];
-    const float r = norm ? rstd[i0 + i] : 1.f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = norm ? ys[i0 + i][8 * cg + e] * r : ys[i0 + i][8 * cg + e];
-    st8v(out + (int64_t)(t0 + i0 + i) * os, y);
-  }
-  __syncthreads();                                 // ys, rstd and this staging buffer free
+  __syncthreads();                                 // this staging buffer free
   }  // tiles
 }
 

@@ -187,20 +187,35 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 }
 
 // The same prologue for 16-bit I/O with 16-byte-aligned rows (what the module
-// passes), head dim HD in {32, 64, 128}: a CTA walks NTL tiles; a tile's input
-// rows (and the three before it, the conv window) arrive in one of two
-// shared-memory buffers by 16-byte cp.async copies issued while the previous
-// tile computes, and a thread owns 8 adjacent channels of a run of TPT tokens, so
-// every global access is 16 bytes per thread -- the thread-per-channel kernel
-// above issues 2-byte accesses, 64 bytes per warp request, and the SM's limit
-// on outstanding requests caps it near 0.6 TB/s.  Tiles of TTV = 32 tokens
-// (fewer registers per thread, more CTAs per SM).  Same rounding points; SiLU
-// uses the fast exponential and divide, whose ~1e-6 relative error vanishes
-// in the rounding of its output to the 16-bit I/O type.
+// passes), head dim HD in {32, 64, 128}: a CTA walks NTL tiles of one tensor
+// and head; a tile's input rows (and the three before it, the conv window)
+// arrive in one of two shared-memory buffers by 16-byte cp.async copies issued
+// while the previous tile computes, and a thread owns 4 adjacent channels of a
+// run of TPT tokens (8-byte shared loads and global stores; a token's HD / 4
+// channel groups are consecutive lanes, so its L2 norm is a shuffle reduction).
+// The thread-per-channel kernel above issues 2-byte accesses, 64 bytes per
+// warp request, and the SM's limit on outstanding requests caps it near
+// 0.6 TB/s.  Tiles of TTV = 32 tokens; 4 channels a thread keep the conv taps
+// in 16 registers (80 a thread, six CTAs an SM).  The grid's y index
+// interleaves the four tensors (q, k, v, gates) head by head, so the cheaper
+// gate CTAs do not all land in the last wave.  Same rounding points; SiLU,
+// sigmoid and softplus use the fast exponential, logarithm and divide, whose
+// ~1e-6 relative error vanishes in the rounding of SiLU's output to the
+// 16-bit I/O type and is far below the fp32 gates' tolerance.
 constexpr int TTV = 32;   // tokens per tile of the vectorised prologue
 constexpr int NTL = 4;    // tiles per CTA: the next tile's copies fly while this one computes
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
+// softplus (threshold 20): log1p(u), u = e^x, by its series to u^7 below
+// u = 1/8 (truncation < u^8 / 8, relative 2^-24) and by log(1 + u) above it
+// (rounding of 1 + u and the fast logarithm: ~1e-6 relative)
+__device__ __forceinline__ float softplus_fast(float x) {
+  const float u = __expf(x);
+  const float ser = u * (1.f - u * (0.5f - u * (1.f / 3 - u * (0.25f - u * (0.2f - u * (1.f / 6 - u * (1.f / 7)))))));
+  const float lg = __logf(1.f + u);
+  return x > 20.f ? x : (u < 0.125f ? ser : lg);
+}
 
 // 16-byte asynchronous copy global -> shared (L2 only); src_bytes = 0 fills zeros
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
@@ -217,58 +232,104 @@ __device__ __forceinline__ void cp_async_wait_prev() {
   asm volatile("cp.async.wait_group 1;" ::: "memory");
 }
 
+
+// N in {4, 8} consecutive values (16-byte or, for N = 4 and 16-bit T, 8-byte
+// aligned) as fp32, and back
+template <int N, typename T>
+__device__ __forceinline__ void ldv(const T* ptr, float (&x)[N]) {
+  if constexpr (N == 8) {
+    ld8v(ptr, x);
+  } else if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(ptr);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(ptr);
+    const uint32_t w[2] = {u.x, u.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float2 f;
+      if constexpr (std::is_same<T, __half>::value)
+        f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      x[2 * i] = f.x;
+      x[2 * i + 1] = f.y;
+    }
+  }
+}
+template <int N, typename T>
+__device__ __forceinline__ void stv(T* ptr, const float (&x)[N]) {
+  if constexpr (std::is_same<T, float>::value) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+      *reinterpret_cast<float4*>(ptr + i) = make_float4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+  } else if constexpr (N == 8) {
+    st8v(ptr, x);
+  } else {
+    uint32_t w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if constexpr (std::is_same<T, __half>::value) {
+        const __half2 hv = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      } else {
+        const __nv_bfloat162 hv = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+    }
+    *reinterpret_cast<uint2*>(ptr) = make_uint2(w[0], w[1]);
+  }
+}
+
 template <typename TIO, typename TG, int HD>
 __global__ void __launch_bounds__(128)
 prologue_vec_kernel(const PrologueParams p) {
-  constexpr int CG = HD / 8, TGRP = 128 / CG, TPT = TTV / TGRP;
+  constexpr int CPT = 4, C8 = HD / 8, CG = HD / CPT, TGRP = 128 / CG, TPT = TTV / TGRP;
   static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
   __shared__ __align__(16) TIO xst[2][TTV + 3][HD];   // input rows t0 - 3 .. t0 + TTV - 1
   const int tid = threadIdx.x, cg = tid % CG, tg = tid / CG;
-  const int lane = tid & 31, warp = tid >> 5;
-  const int tensor = blockIdx.y / p.H, h = blockIdx.y - tensor * p.H;
+  const int tensor = blockIdx.y & 3, h = blockIdx.y >> 2;   // y = 4 h + tensor
   const int b = blockIdx.z;
   const int tile0 = blockIdx.x * NTL;
   const int ntl = min(NTL, (p.T + TTV - 1) / TTV - tile0);
   const int i0 = tg * TPT;                         // first token of this thread in a tile
 
   if (tensor == 3) {                               // decay and beta gates
-    const int ch0 = h * p.K + 8 * cg;
-    float a[8], dtb[8];
+    const int ch0 = h * p.K + CPT * cg;
+    float a[CPT], dtb[CPT];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < CPT; ++e) {
       a[e] = -expf(p.A_log[ch0 + e]);
       dtb[e] = p.dt_bias[ch0 + e];
     }
     const TG* gk = static_cast<const TG*>(p.gk) + b * p.gk_s[0] + ch0;
-    float* g = p.g + b * p.g_s[0] + h * p.g_s[2] + 8 * cg;
+    float* g = p.g + b * p.g_s[0] + h * p.g_s[2] + CPT * cg;
     for (int k = 0; k < ntl; ++k) {
     const int t0 = (tile0 + k) * TTV;
     const int nt = min(TTV, p.T - t0);
-    float gv[TPT][8];
+    float gv[TPT][CPT];
 #pragma unroll
     for (int i = 0; i < TPT; ++i)
-      if (i0 + i < nt) ld8v(gk + (int64_t)(t0 + i0 + i) * p.gk_s[1], gv[i]);
+      if (i0 + i < nt) ldv<CPT>(gk + (int64_t)(t0 + i0 + i) * p.gk_s[1], gv[i]);
 #pragma unroll
     for (int i = 0; i < TPT; ++i) {
       if (i0 + i >= nt) break;
-      float y[8];
+      float y[CPT];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = a[e] * softplus(gv[i][e] + dtb[e]);
-      float* gr = g + (int64_t)(t0 + i0 + i) * p.g_s[1];
-      *reinterpret_cast<float4*>(gr) = make_float4(y[0], y[1], y[2], y[3]);
-      *reinterpret_cast<float4*>(gr + 4) = make_float4(y[4], y[5], y[6], y[7]);
+      for (int e = 0; e < CPT; ++e) y[e] = a[e] * softplus_fast(gv[i][e] + dtb[e]);
+      stv<CPT>(g + (int64_t)(t0 + i0 + i) * p.g_s[1], y);
     }
     for (int i = tid; i < nt; i += blockDim.x) {       // beta: every token of the tile
       const int t = t0 + i;
       const TG* bl = static_cast<const TG*>(p.beta_logit) + b * p.bl_s[0] + (int64_t)t * p.bl_s[1] + h;
-      p.beta[b * p.beta_s[0] + (int64_t)t * p.beta_s[1] + h] = sigmoidf(ld(bl));
+      p.beta[b * p.beta_s[0] + (int64_t)t * p.beta_s[1] + h] = sigmoid_fast(ld(bl));
     }
     }  // tiles
     return;
   }
 
   const int D = tensor == 2 ? p.H * p.V : p.H * p.K;
-  const int ch0 = h * HD + 8 * cg;
+  const int ch0 = h * HD + CPT * cg;
   const TIO* x = static_cast<const TIO*>(tensor == 0 ? p.q_in : tensor == 1 ? p.k_in : p.v_in) +
                  b * p.in_s[tensor][0] + ch0;
   const int64_t xs = p.in_s[tensor][1];
@@ -281,12 +342,12 @@ prologue_vec_kernel(const PrologueParams p) {
   // tile k's rows t0 - 3 .. t0 + TTV - 1 of this head into staging buffer
   // k % 2 by 16-byte asynchronous copies (no registers held while they fly;
   // rows outside the input and the history are zero-filled)
-  const TIO* xh = x - 8 * cg;                      // channel 0 of this head
-  const TIO* hh = hb ? hb - 8 * cg : nullptr;
+  const TIO* xh = x - CPT * cg;                      // channel 0 of this head
+  const TIO* hh = hb ? hb - CPT * cg : nullptr;
   auto stage = [&](int k) {
     const int t0 = (tile0 + k) * TTV, nt = min(TTV, p.T - t0);
-    for (int q = tid; q < (TTV + 3) * CG; q += 128) {
-      const int row = q / CG, c8 = q - row * CG;
+    for (int q = tid; q < (TTV + 3) * C8; q += 128) {
+      const int row = q / C8, c8 = q - row * C8;
       const int i = row - 3, t = t0 + i;
       const TIO* src = xh;
       uint32_t bytes = 0;
@@ -303,16 +364,16 @@ prologue_vec_kernel(const PrologueParams p) {
   stage(0);
   cp_async_commit();
   // taps at the right end of a four-wide window, as in the kernel above
-  float wv[8][4], bv[8];
+  float wv[CPT][4], bv[CPT];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+  for (int e = 0; e < CPT; ++e) {
     bv[e] = bias ? bias[ch0 + e] : 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) wv[e][j] = (j >= 4 - cs) ? w[e * cs + j - (4 - cs)] : 0.f;
   }
   const bool norm = tensor < 2;
   TIO* out = static_cast<TIO*>(tensor == 0 ? p.q : tensor == 1 ? p.k : p.v) +
-             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + 8 * cg;
+             b * p.out_s[tensor][0] + h * p.out_s[tensor][2] + CPT * cg;
   const int64_t os = p.out_s[tensor][1];
   for (int k = 0; k < ntl; ++k) {
   const int t0 = (tile0 + k) * TTV;
@@ -326,20 +387,20 @@ prologue_vec_kernel(const PrologueParams p) {
   // CG channel groups of a token are CG consecutive lanes, so the per-token L2
   // norm is a shuffle reduction (rows past nt are zeros and are not stored).
   {
-    const TIO* xb = &xst[k & 1][i0][8 * cg];
-    float xw[4][8];
+    const TIO* xb = &xst[k & 1][i0][CPT * cg];
+    float xw[4][CPT];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) ld8v(xb + j * HD, xw[j + 1]);
+    for (int j = 0; j < 3; ++j) ldv<CPT>(xb + j * HD, xw[j + 1]);
 #pragma unroll
     for (int i = 0; i < TPT; ++i) {
 #pragma unroll
       for (int j = 0; j < 3; ++j)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xw[j][e] = xw[j + 1][e];
-      ld8v(xb + (i + 3) * HD, xw[3]);
-      float y[8], ss = 0.f;
+        for (int e = 0; e < CPT; ++e) xw[j][e] = xw[j + 1][e];
+      ldv<CPT>(xb + (i + 3) * HD, xw[3]);
+      float y[CPT], ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 0; e < CPT; ++e) {
         float acc = bv[e];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -352,9 +413,9 @@ prologue_vec_kernel(const PrologueParams p) {
         for (int off = 1; off < CG; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float r = fminf(rsqrtf(ss), 1.f / p.eps);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] *= r;
+        for (int e = 0; e < CPT; ++e) y[e] *= r;
       }
-      if (i0 + i < nt) st8v(out + (int64_t)(t0 + i0 + i) * os, y);
+      if (i0 + i < nt) stv<CPT>(out + (int64_t)(t0 + i0 + i) * os, y);
     }
   }
   // new conv cache: the last keep inputs of cat(history, x)
@@ -364,7 +425,7 @@ prologue_vec_kernel(const PrologueParams p) {
     for (int j = 0; j < keep; ++j) {
       const int t = p.T - keep + j;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
+      for (int e = 0; e < CPT; ++e) {
         const float v = t >= 0 ? ld(x + (int64_t)t * xs + e)
                                : (hb != nullptr ? ld(hb + (int64_t)(keep + t) * D + e) : 0.f);
         st(nc + (int64_t)j * D + e, v);
@@ -449,57 +510,72 @@ static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-// The epilogue for 16-bit I/O with V = 128 and 8-byte-aligned rows: lane l
-// owns channels 4l .. 4l + 3, one 8-byte access per tensor and row (the kernel
-// above makes four 2-byte accesses, 64 bytes per warp request).
+// The epilogue for 16-bit I/O with V = 128 and 16-byte-aligned rows: a half
+// warp owns one (b, t, h) row, lane l of it channels 8l .. 8l + 7 (one 16-byte
+// access per tensor and row), and a warp walks EPI_ROWS rows whose loads are
+// all issued before the first row computes, so each thread keeps
+// EPI_ROWS / 2 x 32 bytes in flight (the scalar kernel above makes 2-byte
+// accesses, one row per warp).  Same rounding points; the gate's sigmoid uses
+// the fast exponential and divide (~1e-6 relative, below the output's 16-bit
+// rounding).
+constexpr int EPI_ROWS = 8;   // rows per warp of the vectorised epilogue
+
 template <typename TIO>
 __global__ void __launch_bounds__(256)
 epilogue_vec_kernel(const EpilogueParams p) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  constexpr int NI = EPI_ROWS / 2;
+  const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31, half = lane >> 4, c = lane & 15;
   const long rows = (long)p.B * p.T * p.H;
-  if (warp >= rows) return;
-  const int h = warp % p.H;
-  const long bt = warp / p.H;
-  const int t = (int)(bt % p.T), b = (int)(bt / p.T);
-  const TIO* o = static_cast<const TIO*>(p.o) + b * p.o_s[0] + (int64_t)t * p.o_s[1] + h * p.o_s[2];
-  const TIO* og = static_cast<const TIO*>(p.og) + b * p.og_s[0] + (int64_t)t * p.og_s[1] + h * 128;
-  TIO* y = static_cast<TIO*>(p.y) + b * p.y_s[0] + (int64_t)t * p.y_s[1] + h * 128;
-  auto ld4 = [](const TIO* ptr, float (&x)[4]) {
-    const uint2 u = *reinterpret_cast<const uint2*>(ptr);
-    float2 a, c;
-    if constexpr (std::is_same<TIO, __half>::value) {
-      a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-      c = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-    } else {
-      a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-    }
-    x[0] = a.x; x[1] = a.y; x[2] = c.x; x[3] = c.y;
+  const long r0 = warp * EPI_ROWS + half;
+  if (warp * EPI_ROWS >= rows) return;
+  // (b, t, h) of row r0; the row two further on is h + 2 with carries into t, b
+  const int h0 = (int)(r0 % p.H);
+  const long bt0 = r0 / p.H;
+  const int t0 = (int)(bt0 % p.T), b0 = (int)(bt0 / p.T);
+  auto next = [&](int& b, int& t, int& h) {
+    for (h += 2; h >= p.H; h -= p.H)
+      if (++t == p.T) { t = 0; ++b; }
   };
-  float xv[4], gv[4];
-  ld4(o + 4 * lane, xv);
-  ld4(og + 4 * lane, gv);
-  float ss = 0.f;
+  uint4 xo[NI], xg[NI];
+  {
+    int b = b0, t = t0, h = h0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) ss = fmaf(xv[j], xv[j], ss);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float r = rsqrtf(ss / 128.f + p.eps);
-  const float4 w = *reinterpret_cast<const float4*>(p.weight + h * 128 + 4 * lane);
-  const float wv[4] = {w.x, w.y, w.z, w.w};
-  float out[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) out[j] = rnd<TIO>(xv[j] * r * wv[j]) * sigmoidf(gv[j]);
-  uint2 u;
-  if constexpr (std::is_same<TIO, __half>::value) {
-    const __half2 a = __floats2half2_rn(out[0], out[1]), c = __floats2half2_rn(out[2], out[3]);
-    u = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&c));
-  } else {
-    const __nv_bfloat162 a = __floats2bfloat162_rn(out[0], out[1]);
-    const __nv_bfloat162 c = __floats2bfloat162_rn(out[2], out[3]);
-    u = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&c));
+    for (int i = 0; i < NI; ++i) {
+      if (i > 0) next(b, t, h);
+      xo[i] = make_uint4(0u, 0u, 0u, 0u);
+      xg[i] = xo[i];
+      if (r0 + 2 * i < rows) {
+        xo[i] = *reinterpret_cast<const uint4*>(static_cast<const TIO*>(p.o) + b * p.o_s[0] +
+                                                (int64_t)t * p.o_s[1] + h * p.o_s[2] + 8 * c);
+        xg[i] = *reinterpret_cast<const uint4*>(static_cast<const TIO*>(p.og) + b * p.og_s[0] +
+                                                (int64_t)t * p.og_s[1] + h * 128 + 8 * c);
+      }
+    }
   }
-  *reinterpret_cast<uint2*>(y + 4 * lane) = u;
+  int b = b0, t = t0, h = h0;
+#pragma unroll
+  for (int i = 0; i < NI; ++i) {
+    if (i > 0) next(b, t, h);
+    float xv[8], gv[8];
+    ld8v(reinterpret_cast<const TIO*>(&xo[i]), xv);
+    ld8v(reinterpret_cast<const TIO*>(&xg[i]), gv);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(xv[j], xv[j], ss);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (r0 + 2 * i >= rows) continue;
+    const float rs = rsqrtf(ss / 128.f + p.eps);
+    const float* w = p.weight + h * 128 + 8 * c;
+    const float4 w0 = *reinterpret_cast<const float4*>(w);
+    const float4 w1 = *reinterpret_cast<const float4*>(w + 4);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = rnd<TIO>(xv[j] * rs * wv[j]) * sigmoid_fast(gv[j]);
+    st8v(static_cast<TIO*>(p.y) + b * p.y_s[0] + (int64_t)t * p.y_s[1] + h * 128 + 8 * c, out);
+  }
 }
 
 template <typename TIO>
@@ -523,20 +599,20 @@ cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s) {
   const long rows = (long)p.B * p.T * p.H;
   const int threads = 256;
   const long blocks = (rows * 32 + threads - 1) / threads;
-  auto al8 = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 8 == 0; };
-  const bool vec = p.io_dtype != KDA_DTYPE_F32 && p.V == 128 && al8(p.o) && al8(p.og) &&
-                   al8(p.y) && reinterpret_cast<uintptr_t>(p.weight) % 16 == 0 &&
-                   p.o_s[0] % 4 == 0 && p.o_s[1] % 4 == 0 && p.o_s[2] % 4 == 0 &&
-                   p.og_s[0] % 4 == 0 && p.og_s[1] % 4 == 0 && p.y_s[0] % 4 == 0 &&
-                   p.y_s[1] % 4 == 0;
+  auto al16 = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  const bool vec = p.io_dtype != KDA_DTYPE_F32 && p.V == 128 && al16(p.o) && al16(p.og) &&
+                   al16(p.y) && al16(p.weight) && p.o_s[0] % 8 == 0 && p.o_s[1] % 8 == 0 &&
+                   p.o_s[2] % 8 == 0 && p.og_s[0] % 8 == 0 && p.og_s[1] % 8 == 0 &&
+                   p.y_s[0] % 8 == 0 && p.y_s[1] % 8 == 0;
+  const long vblocks = (rows + io::EPI_ROWS * (threads / 32) - 1) / (io::EPI_ROWS * (threads / 32));
   switch (p.io_dtype) {
     case KDA_DTYPE_F32: io::epilogue_kernel<float><<<blocks, threads, 0, s>>>(p); break;
     case KDA_DTYPE_F16:
-      if (vec) io::epilogue_vec_kernel<__half><<<blocks, threads, 0, s>>>(p);
+      if (vec) io::epilogue_vec_kernel<__half><<<vblocks, threads, 0, s>>>(p);
       else io::epilogue_kernel<__half><<<blocks, threads, 0, s>>>(p);
       break;
     default:
-      if (vec) io::epilogue_vec_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p);
+      if (vec) io::epilogue_vec_kernel<__nv_bfloat16><<<vblocks, threads, 0, s>>>(p);
       else io::epilogue_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p);
       break;
   }

@@ -761,7 +761,8 @@ def profile_case(which, reps=3):
     """Three calls of one workload on cuda:0 (the target of the ncu captures
     summarised under profiles/): ``prefill`` = configs[1], ``decode`` = one
     configs[2] step, ``mla`` = one configs[4] MLA decode step (8192-token
-    prompt in the static buffer)."""
+    prompt in the static buffer), ``io`` = the fused prologue then the fused
+    epilogue at the configs[1] shape (the inputs of ``bench_fused_io``)."""
     import torch
     kb = importlib.import_module("-kimi-linear-_b200")
     kb.load_library()
@@ -771,6 +772,24 @@ def profile_case(which, reps=3):
         for _ in range(reps):
             kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=CFG1["C"],
                              state_dtype=torch.float32)
+    elif which == "io":
+        B, T, H, K = 1, CFG1["T"], CFG1["H"], CFG1["K"]
+        D = H * K
+        g = torch.Generator(device=dev).manual_seed(5)
+        x = {n: torch.randn(B, T, D, generator=g, device=dev).half() for n in ("q", "k", "v", "gk")}
+        bl = torch.randn(B, T, H, generator=g, device=dev).half()
+        ws = [(torch.randn(D, 1, 4, generator=g, device=dev) * 0.4).half().float()
+              for _ in range(3)]
+        bs = [(torch.randn(D, generator=g, device=dev) * 0.1).half().float() for _ in range(3)]
+        A_log = torch.log(torch.rand(H, K, generator=g, device=dev) * 15 + 1)
+        dt_bias = torch.log(torch.expm1(torch.rand(H, K, generator=g, device=dev) * 0.099 + 1e-3))
+        for _ in range(reps):
+            kb.kda_prologue(x["q"], x["k"], x["v"], x["gk"], bl, ws, bs, A_log, dt_bias, H, K, K,
+                            1e-6)
+        o = torch.randn(B, T, H, K, generator=g, device=dev).half()
+        w = torch.rand(H, K, generator=g, device=dev) + 0.5
+        for _ in range(reps):
+            kb.kda_epilogue(o, x["q"], w, 1e-6)
     elif which == "mla":
         c = CFG4_MLA
         B, L, H, KVL, DN, DV = c["B"], c["L"], c["H"], c["KVL"], c["DN"], c["DV"]
@@ -809,7 +828,7 @@ def main():
     ap.add_argument("--bwd-steps", type=int, default=6,
                     help="timed calls of the configs[1] backward leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=("prefill", "decode", "mla"),
+    ap.add_argument("--case", choices=("prefill", "decode", "mla", "io"),
                     help="profiling target: run the workload three times, print nothing timed")
     a = ap.parse_args()
     if a.case:

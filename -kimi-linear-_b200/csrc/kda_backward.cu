@@ -408,8 +408,12 @@ static cudaError_t launch_si(const BwdParams& p, cudaStream_t s) {
 
 }  // namespace bwd
 
+// the token-serial kernels need one state per 64-step chunk; the chunkwise
+// path (V <= 128) needs its per-chunk records, which include those states
 size_t backward_ckpt_floats(int B, int H, int T, int K, int V) {
-  return (size_t)B * H * ((T + bwd::CK - 1) / bwd::CK) * K * V;
+  const size_t serial = (size_t)B * H * ((T + bwd::CK - 1) / bwd::CK) * K * V;
+  const size_t chunk = V <= 128 ? backward_chunk_ws_floats(B, H, T, K, V) : 0;
+  return serial > chunk ? serial : chunk;
 }
 
 namespace bwd {

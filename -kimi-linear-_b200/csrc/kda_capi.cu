@@ -245,8 +245,12 @@ int validate_backward(const KdaBackwardArgs* a) {
   if (!dtype_ok(a->io_dtype)) return KDA_ERR_DTYPE;
   if (a->state_in != nullptr && !dtype_ok(a->state_in_dtype)) return KDA_ERR_DTYPE;
   if (a->B == 0 || a->H == 0 || a->T == 0) return KDA_OK;
-  if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->dout || !a->dq_part || !a->dk_part ||
-      !a->dg_part || !a->dbeta_part || !a->dv || !a->ckpt)
+  if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->dout || !a->dv || !a->ckpt)
+    return KDA_ERR_NULL_POINTER;
+  // the partial sums are needed unless the chunkwise path (dq set, V <= 128)
+  // writes the final gradients itself
+  const bool chunkwise = a->dq != nullptr && a->V <= 128;
+  if (!chunkwise && (!a->dq_part || !a->dk_part || !a->dg_part || !a->dbeta_part))
     return KDA_ERR_NULL_POINTER;
   if (a->q_stride[3] != 1 || a->k_stride[3] != 1 || a->v_stride[3] != 1 || a->g_stride[3] != 1 ||
       a->dout_stride[3] != 1 || a->dv_stride[3] != 1)
@@ -398,8 +402,13 @@ int kda_backward(const KdaBackwardArgs* args, void* stream) {
   if (st != KDA_OK) return st;
   const BwdParams p = to_backward(args);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = launch_backward(p, s);
-  if (e == cudaSuccess && p.dq != nullptr) e = launch_backward_reduce(p, s);
+  cudaError_t e;
+  if (backward_chunk_supported(p)) {
+    e = launch_backward_chunk(p, s);
+  } else {
+    e = launch_backward(p, s);
+    if (e == cudaSuccess && p.dq != nullptr) e = launch_backward_reduce(p, s);
+  }
   return launch_status(e);
 }
 

@@ -128,6 +128,12 @@ size_t backward_ckpt_floats(int B, int H, int T, int K, int V);
 cudaError_t launch_backward(const BwdParams& p, cudaStream_t s);
 // dq, dk, dg, dbeta = sums of the V/16 partials (after launch_backward)
 cudaError_t launch_backward_reduce(const BwdParams& p, cudaStream_t s);
+// chunkwise backward (kda_backward_chunk.cu): writes dq, dk, dv, dg, dbeta and
+// dstate_in directly (no partials); needs dq set, V <= 128 and a workspace of
+// backward_chunk_ws_floats() floats in ckpt
+bool backward_chunk_supported(const BwdParams& p);
+size_t backward_chunk_ws_floats(int B, int H, int T, int K, int V);
+cudaError_t launch_backward_chunk(const BwdParams& p, cudaStream_t s);
 
 cudaError_t launch_prologue(const PrologueParams& p, cudaStream_t s);
 cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s);

@@ -277,9 +277,10 @@ def kda_backward(q, k, v, g, beta, state, do, dS):
     ``q``, ``k``, ``v`` share one dtype; ``g``, ``beta`` fp32; ``state`` is
     None (zero initial state, ``dstate`` None) or [B, H, K, V] in any
     supported dtype.  dq, dk, dv come back in v's dtype, dg and dbeta fp32,
-    dstate in ``state``'s dtype.  Reduction over V tiles: the kernel writes
-    per-16-column partial sums of dq, dk, dg and dbeta, which the library sums
-    into the final gradients in the same call."""
+    dstate in ``state``'s dtype.  For V <= 128 the library runs the chunkwise
+    backward (64-token chunks in parallel, two short state chains); wider V
+    runs the token-serial kernels, whose per-16-column partial sums the library
+    adds up in the same call."""
     fn = "kda_backward"
     dev = _check_tensors(fn, [("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
                               ("state", state), ("do", do), ("dS", dS)])
@@ -302,17 +303,22 @@ def kda_backward(q, k, v, g, beta, state, do, dS):
     dv = torch.empty(B, T, H, V, device=dev, dtype=torch.float32)
     dstate = (torch.empty(B, H, K, V, device=dev, dtype=torch.float32)
               if state is not None else None)
-    nvt = max(V // 16, 1)
-    dq_p = torch.empty(nvt, B, T, H, K, device=dev, dtype=torch.float32)
-    dk_p = torch.empty_like(dq_p)
-    dg_p = torch.empty_like(dq_p)
-    db_p = torch.empty(nvt, B, T, H, device=dev, dtype=torch.float32)
     if B * T * H == 0:
         if dstate is not None:
             dstate.copy_(dS if dS is not None else torch.zeros_like(dstate))
-        z = dq_p.sum(0)
-        return (z.to(io), z.to(io), dv.zero_().to(io), z, db_p.sum(0),
+        z = torch.zeros(B, T, H, K, device=dev, dtype=torch.float32)
+        return (z.to(io), z.to(io), dv.zero_().to(io), z,
+                torch.zeros(B, T, H, device=dev, dtype=torch.float32),
                 None if state is None else dstate.to(state.dtype))
+    # V <= 128: the chunkwise kernels write the final gradients; wider V runs
+    # the token-serial kernels, which write per-16-column partial sums that the
+    # library then adds up (both in the same call)
+    if V > 128:
+        nvt = V // 16
+        dq_p = torch.empty(nvt, B, T, H, K, device=dev, dtype=torch.float32)
+        dk_p = torch.empty_like(dq_p)
+        dg_p = torch.empty_like(dq_p)
+        db_p = torch.empty(nvt, B, T, H, device=dev, dtype=torch.float32)
     lib = _lib.load()
     ck_n = int(lib.kda_backward_ckpt_floats(B, H, T, K, V))
     ckpt = torch.empty(max(ck_n, 4), device=dev, dtype=torch.float32)
@@ -335,11 +341,11 @@ def kda_backward(q, k, v, g, beta, state, do, dS):
     a.dout, a.dout_stride = do.data_ptr(), _strides(do, 4)
     if dS is not None:
         a.dstate_out, a.dstate_out_stride = dS.data_ptr(), _strides(dS, 4)
-    a.dq_part, a.dk_part = dq_p.data_ptr(), dk_p.data_ptr()
-    a.dg_part, a.dbeta_part = dg_p.data_ptr(), db_p.data_ptr()
+    if V > 128:
+        a.dq_part, a.dk_part = dq_p.data_ptr(), dk_p.data_ptr()
+        a.dg_part, a.dbeta_part = dg_p.data_ptr(), db_p.data_ptr()
     a.dv, a.dv_stride = dv.data_ptr(), _strides(dv, 4)
     a.ckpt, a.ckpt_floats = ckpt.data_ptr(), ck_n
-    # the library sums the partials into the final gradients (same stream)
     dq = torch.empty(B, T, H, K, device=dev, dtype=io)
     dk = torch.empty_like(dq)
     dg = torch.empty(B, T, H, K, device=dev, dtype=torch.float32)

@@ -691,8 +691,9 @@ def bench_long_context(torch, kb, dev, steps, warmup, dist, world, rank, clk):
 def bench_backward(torch, kb, dev, steps, warmup, clk):
     """configs[1] backward: the gradients of one ``kda_chunkwise`` call (B=1,
     T=4096, H=16, fp16 q/k/v, fp32 state) for random output and final-state
-    gradients, through ``ops.kda_backward`` (checkpoint pass, reverse sweep and
-    the partial-sum reduction, all in the library).  Two rotating input sets.
+    gradients, through ``ops.kda_backward`` (the chunkwise backward: per-chunk
+    prep, the two state chains in one launch, the per-chunk gradients).  Two
+    rotating input sets.
     Returns (ms per call, algorithmic bytes: every input read once and every
     gradient written once)."""
     B, T, H, K, V = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"], CFG1["V"]
@@ -762,7 +763,8 @@ def profile_case(which, reps=3):
     summarised under profiles/): ``prefill`` = configs[1], ``decode`` = one
     configs[2] step, ``mla`` = one configs[4] MLA decode step (8192-token
     prompt in the static buffer), ``io`` = the fused prologue then the fused
-    epilogue at the configs[1] shape (the inputs of ``bench_fused_io``)."""
+    epilogue at the configs[1] shape (the inputs of ``bench_fused_io``),
+    ``bwd`` = the configs[1] backward of ``bench_backward``."""
     import torch
     kb = importlib.import_module("-kimi-linear-_b200")
     kb.load_library()
@@ -772,6 +774,14 @@ def profile_case(which, reps=3):
         for _ in range(reps):
             kb.kda_chunkwise(x["q"], x["k"], x["v"], x["g"], x["beta"], chunk_size=CFG1["C"],
                              state_dtype=torch.float32)
+    elif which == "bwd":
+        B, T, H, K, V = CFG1["B"], CFG1["T"], CFG1["H"], CFG1["K"], CFG1["V"]
+        gen = torch.Generator(device=dev).manual_seed(9)
+        x = kb.synth.make_config(1, seed=20, device=dev)
+        do = torch.randn(B, T, H, V, generator=gen, device=dev).half()
+        dS = torch.randn(B, H, K, V, generator=gen, device=dev) * 0.01
+        for _ in range(reps):
+            kb.ops.kda_backward(x["q"], x["k"], x["v"], x["g"], x["beta"], None, do, dS)
     elif which == "io":
         B, T, H, K = 1, CFG1["T"], CFG1["H"], CFG1["K"]
         D = H * K
@@ -828,7 +838,7 @@ def main():
     ap.add_argument("--bwd-steps", type=int, default=6,
                     help="timed calls of the configs[1] backward leg (0 skips it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=("prefill", "decode", "mla", "io"),
+    ap.add_argument("--case", choices=("prefill", "decode", "mla", "io", "bwd"),
                     help="profiling target: run the workload three times, print nothing timed")
     a = ap.parse_args()
     if a.case:
@@ -1007,14 +1017,17 @@ def main():
             "backward": None if bwd is None else {
                 "workload": "gradients of one kda_chunkwise call at configs[1] (B=1, T=4096, "
                             "H=16, fp16, fp32 state) for random do and dS, ops.kda_backward "
-                            "(checkpoint pass, reverse sweep, partial-sum reduction)",
+                            "(chunkwise: per-chunk prep, forward and reverse state chains, "
+                            "per-chunk gradients; fp32 data, 3xTF32 mma.sync GEMMs)",
                 "value": tokens / (bwd[0] * 1e-3), "unit": "tokens/s",
                 "ms_per_call": bwd[0],
                 "roofline": {"bound": "hbm", "achieved": bwd[1] / (bwd[0] * 1e-3) / 1e9,
                              "peak": hbm, "unit": "GB/s",
                              "frac": bwd[1] / (bwd[0] * 1e-3) / 1e9 / hbm,
                              "algorithmic_bytes": bwd[1],
-                             "note": "token-serial reverse sweep, instruction-bound"}},
+                             "note": "compute-bound (fp32 GEMMs as 3xTF32 mma.sync, one "
+                                     "exponential per pair and channel); the HBM fraction is "
+                                     "for reference"}},
             "configs4_decode": {
                 "workload": "configs[4] decode step, attention side at its layer shapes "
                             "(B=4, fp16): 18 KDA layers x (fused prologue + recurrent "

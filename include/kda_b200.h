@@ -246,8 +246,13 @@ int kda_epilogue_fwd(const KdaEpilogueArgs* args, void* stream);
  *   dbeta_part : [V/16, B, T, H] fp32 partial sums
  *   ckpt       : workspace of kda_backward_ckpt_floats() fp32 values
  *   dq, dk     : [B, T, H, K] in io_dtype, or NULL; when dq is set, the call
- *                also sums the partials into dq, dk, dg ([B, T, H, K] fp32)
- *                and dbeta ([B, T, H] fp32) on the same stream
+ *                also writes dq, dk, dg ([B, T, H, K] fp32) and dbeta
+ *                ([B, T, H] fp32) on the same stream
+ * With dq set and V <= 128 the call runs the chunkwise backward (64-token
+ * chunks in parallel, the chunk-boundary states and their gradients by two
+ * chains), writes the final gradients directly and ignores the partial-sum
+ * pointers, which may be NULL.  Otherwise it runs the token-serial reverse
+ * sweep into the partials (and sums them when dq is set).
  * Requires K in {32, 64, 128} and V % 16 == 0.
  */
 typedef struct KdaBackwardArgs {
@@ -280,7 +285,9 @@ typedef struct KdaBackwardArgs {
 
 int kda_backward(const KdaBackwardArgs* args, void* stream);
 
-/* fp32 values of the backward checkpoint workspace: B * H * ceil(T/64) * K * V. */
+/* fp32 values of the backward workspace: for V <= 128 the chunkwise records,
+ * B * H * ceil(T/64) * (4*64*64 + 5*64*K + K + 2*K*V); for wider V the
+ * token-serial checkpoints, B * H * ceil(T/64) * K * V. */
 size_t kda_backward_ckpt_floats(int B, int H, int T, int K, int V);
 
 /* sizeof(KdaBackwardArgs) as compiled. */

@@ -145,6 +145,11 @@ __device__ __forceinline__ void wgemm3(float (&acc)[MT][NT][4], const float* A, 
     }
   }
 }
+// (row, column) of element e of a thread's accumulator tile at (m0, n0 + 8 nt)
+__device__ __forceinline__ int acc_row(int m0, int lane, int e) { return m0 + (lane >> 2) + 8 * (e >> 1); }
+__device__ __forceinline__ int acc_col(int n0, int nt, int lane, int e) {
+  return n0 + 8 * nt + 2 * (lane & 3) + (e & 1);
+}
 template <int MT, int NT>
 __device__ __forceinline__ void zero(float (&acc)[MT][NT][4]) {
 #pragma unroll
@@ -171,7 +176,8 @@ struct PrepSmem {
   static constexpr int TS = LS + C * (C + 1);
   static constexpr int END = GT + KD * LD > TS + C * (C + 1) ? GT + KD * LD : TS + C * (C + 1);
   static constexpr int BS = END;                    // beta [C]
-  static constexpr int FLOATS = BS + C;
+  static constexpr int STP = BS + C;                // steep-block bits of each channel [KD]
+  static constexpr int FLOATS = STP + KD;
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
 };
 
@@ -186,7 +192,8 @@ prep_kernel(const BwdParams p, float* __restrict__ ws) {
   float* Ls = sm + L::LS;
   float* Ts = sm + L::TS;
   float* bs = sm + L::BS;
-  const int tid = threadIdx.x;
+  unsigned* STP = reinterpret_cast<unsigned*>(sm + L::STP);
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int NC = num_chunks(p.T);
   const Rec R{KD, p.V};
@@ -211,11 +218,25 @@ prep_kernel(const BwdParams p, float* __restrict__ ws) {
   }
   __syncthreads();
   if (tid < KD) {                                   // cumulative log decay, fp32
-    float G = 0.f;
+    // and the channel's steep blocks: block I (anchor a = 16 I) is steep when a
+    // factor exp(G_i - G_a) (i in I) or exp(G_a - G_j) (j < a + 16) leaves
+    // e^-80 .. e^80
+    float G = 0.f, runmin = 0.f, ga = 0.f, bmin = 0.f, bmax = 0.f;
+    unsigned bits = 0u;
     for (int i = 0; i < C; ++i) {
       G += gT[tid * L::LD + i];
       gT[tid * L::LD + i] = G;
+      if ((i & 15) == 0) {
+        ga = G;
+        bmin = bmax = G;
+      }
+      bmin = fminf(bmin, G);
+      bmax = fmaxf(bmax, G);
+      runmin = i == 0 ? G : fminf(runmin, G);
+      if ((i & 15) == 15 && (bmin - ga < -80.f || bmax - ga > 80.f || ga - runmin > 80.f))
+        bits |= 1u << (i >> 4);
     }
+    STP[tid] = bits;
   }
   __syncthreads();
 
@@ -232,54 +253,85 @@ prep_kernel(const BwdParams p, float* __restrict__ ws) {
   }
   if (tid < KD) rec[R.gcv() + tid] = expf(gT[tid * L::LD + C - 1]);
 
-  // pair sums: thread (row i, 16-column block jb) of the lower triangle
+  // pair sums by anchored 16-row blocks (3xTF32 mma.sync): for rows i of
+  // block I (anchor a = 16 I), exp(G_ic - G_jc) = exp(G_ic - G_ac) exp(G_ac - G_jc).
+  // The 20 tiles (block I, 8 columns) of the lower block triangle go round the
+  // warps; A(i, c) = k_ic exp(G_ic - G_ac) (Lraw) and q'_ic exp(G_ic - G_ac)
+  // (Mq), B(c, j) = k_jc exp(G_ac - G_jc).  Channels for which block I is steep
+  // are left out and added exactly below.
+  float* lraw = rec + R.lraw();
+  float* mqg = rec + R.mq();
   {
-    const int i = tid >> 2, jb = tid & 3;
-    float lr[16], mq[16];
-#pragma unroll
-    for (int m = 0; m < 16; ++m) lr[m] = mq[m] = 0.f;
-    if (16 * jb <= i) {
+    const int g = lane >> 2, tq = lane & 3;
+    for (int q = w; q < 20; q += NW) {
+      const int I = q < 2 ? 0 : q < 6 ? 1 : q < 12 ? 2 : 3;
+      const int j0 = 8 * (q - (I == 0 ? 0 : I == 1 ? 2 : I == 2 ? 6 : 12));
+      const int a = 16 * I;
+      float al[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-      for (int c = 0; c < KD; ++c) {
-        const float* kr = kT + c * L::LD;
-        const float* gr = gT + c * L::LD;
-        const float ki = kr[i], qi = qT[c * L::LD + i], Gi = gr[i];
+      for (int kc = 0; kc < KD; kc += 8) {
+        uint32_t kh[4], kl[4], qh[4], ql[4], bh[2], bl[2];
 #pragma unroll
-        for (int m4 = 0; m4 < 4; ++m4) {
-          const float4 kj = lds4(kr + 16 * jb + 4 * m4);
-          const float4 Gj = lds4(gr + 16 * jb + 4 * m4);
-          const float kja[4] = {kj.x, kj.y, kj.z, kj.w};
-          const float Gja[4] = {Gj.x, Gj.y, Gj.z, Gj.w};
+        for (int e = 0; e < 4; ++e) {                // A(i, c): rows a + g (+8), channels kc + tq (+4)
+          const int i = a + g + 8 * (e & 1), c = kc + tq + 4 * (e >> 1);
+          const bool st = (STP[c] >> I) & 1u;
+          const float wa = st ? 0.f : __expf(gT[c * L::LD + i] - gT[c * L::LD + a]);
+          split3(kT[c * L::LD + i] * wa, kh[e], kl[e]);
+          split3(qT[c * L::LD + i] * wa, qh[e], ql[e]);
+        }
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = 4 * m4 + e;
-            if (16 * jb + m <= i) {
-              const float t = kja[e] * __expf(Gi - Gja[e]);
-              lr[m] = fmaf(ki, t, lr[m]);
-              mq[m] = fmaf(qi, t, mq[m]);
-            }
-          }
+        for (int e = 0; e < 2; ++e) {                // B(c, j): channels kc + tq (+4), column j0 + g
+          const int c = kc + tq + 4 * e, j = j0 + g;
+          const bool st = (STP[c] >> I) & 1u;
+          const float wb = st ? 0.f : __expf(gT[c * L::LD + a] - gT[c * L::LD + j]);
+          split3(kT[c * L::LD + j] * wb, bh[e], bl[e]);
+        }
+        ptx::mma_tf32_16x8x8(al, kl, bh);
+        ptx::mma_tf32_16x8x8(al, kh, bl);
+        ptx::mma_tf32_16x8x8(al, kh, bh);
+        ptx::mma_tf32_16x8x8(am, ql, bh);
+        ptx::mma_tf32_16x8x8(am, qh, bl);
+        ptx::mma_tf32_16x8x8(am, qh, bh);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = acc_row(a, lane, e), j = acc_col(j0, 0, lane, e);
+        lraw[i * C + j] = j < i ? al[e] : 0.f;
+        mqg[i * C + j] = j <= i ? am[e] : 0.f;
+      }
+    }
+    // the rest of each row block (columns past the block) is zero
+    for (int e = tid; e < C * C; e += NTH) {
+      const int i = e / C, j = e - i * C;
+      if (j >= 16 * ((i >> 4) + 1)) {
+        lraw[e] = 0.f;
+        mqg[e] = 0.f;
+      }
+    }
+  }
+  __syncthreads();
+  // steep blocks: exact pair terms of the left-out channels (rare)
+  for (int x = tid; x < 2 * KD; x += NTH) {
+    const int c = x % KD, half = x / KD;
+    const unsigned bits = STP[c];
+    if (bits == 0u) continue;
+    for (int I = 0; I < 4; ++I) {
+      if (!((bits >> I) & 1u)) continue;
+      for (int i = 16 * I + half; i < 16 * I + 16; i += 2) {
+        const float Gi = gT[c * L::LD + i], ki = kT[c * L::LD + i], qi = qT[c * L::LD + i];
+        for (int j = 0; j <= i; ++j) {
+          const float t = kT[c * L::LD + j] * __expf(Gi - gT[c * L::LD + j]);
+          if (j < i) atomicAdd(&lraw[i * C + j], ki * t);
+          atomicAdd(&mqg[i * C + j], qi * t);
         }
       }
     }
-    __syncthreads();                                // [c][i] arrays dead from here
-    for (int e = tid; e < C * (C + 1); e += NTH) Ts[e] = 0.f;
-    const float bi = bs[i];
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int j = 16 * jb + m;
-      if (j >= i) lr[m] = 0.f;                      // strictly lower
-      Ls[i * (C + 1) + j] = bi * lr[m];
-    }
-    float* lrow = rec + R.lraw() + (size_t)i * C + 16 * jb;
-    float* mrow = rec + R.mq() + (size_t)i * C + 16 * jb;
-#pragma unroll
-    for (int m4 = 0; m4 < 4; ++m4) {
-      *reinterpret_cast<float4*>(lrow + 4 * m4) =
-          make_float4(lr[4 * m4], lr[4 * m4 + 1], lr[4 * m4 + 2], lr[4 * m4 + 3]);
-      *reinterpret_cast<float4*>(mrow + 4 * m4) =
-          make_float4(mq[4 * m4], mq[4 * m4 + 1], mq[4 * m4 + 2], mq[4 * m4 + 3]);
-    }
+  }
+  __syncthreads();                                  // the [c][i] arrays are dead from here
+  for (int e = tid; e < C * (C + 1); e += NTH) Ts[e] = 0.f;
+  for (int e = tid; e < C * C; e += NTH) {
+    const int i = e / C, j = e - i * C;
+    Ls[i * (C + 1) + j] = bs[i] * lraw[e];
   }
   __syncthreads();
 
@@ -317,11 +369,6 @@ struct StateTile {
   static constexpr int WPM = 4 / NT;               // warps per 16-row m-tile
 };
 
-// (row, column) of element e of a thread's accumulator tile at (m0, n0 + 8 nt)
-__device__ __forceinline__ int acc_row(int m0, int lane, int e) { return m0 + (lane >> 2) + 8 * (e >> 1); }
-__device__ __forceinline__ int acc_col(int n0, int nt, int lane, int e) {
-  return n0 + 8 * nt + 2 * (lane & 3) + (e & 1);
-}
 
 template <int KD>
 struct FchainSmem {
@@ -675,6 +722,7 @@ chains_kernel(const BwdParams p, float* __restrict__ ws) {
 constexpr int VMAX = 128;
 constexpr int VS = VMAX + 4;                       // row stride of the [*][v] arrays (k = v)
 constexpr int LDK = 33;                            // row stride of the [i][c] channel slices
+constexpr int LDL = C + 4;                         // row stride of beta dL and dMq
 
 struct GradSmem {
   static constexpr int DRS = 0;                    // dR [C][VS]
@@ -682,9 +730,9 @@ struct GradSmem {
   static constexpr int DOS = PS + C * VS;          // dO [C][VS]
   static constexpr int SS = DOS + C * VS;          // S rows of a 32-channel slice [32][VS]
   static constexpr int DSS = SS + 32 * VS;         // dS_next rows [32][VS]
-  static constexpr int LR = DSS + 32 * VS;         // beta dL (j < i) [C][C]
-  static constexpr int MQD = LR + C * C;           // dMq (j <= i) [C][C]
-  static constexpr int QS = MQD + C * C;           // q' [C][LDK]
+  static constexpr int LR = DSS + 32 * VS;         // beta dL (j < i) [C][LDL]
+  static constexpr int MQD = LR + C * LDL;         // dMq (j <= i) [C][LDL]
+  static constexpr int QS = MQD + C * LDL;         // q' [C][LDK]
   static constexpr int KS = QS + C * LDK;          // k
   static constexpr int GS = KS + C * LDK;          // G
   static constexpr int E8 = GS + C * LDK;          // dEQ, then dG
@@ -692,10 +740,12 @@ struct GradSmem {
   static constexpr int KB8 = KG8 + C * LDK;        // dKbar
   static constexpr int RED = KB8 + C * LDK;        // [2][NW][32] column partial sums
   static constexpr int DB = RED + 2 * NW * 32;     // dbeta [3][C]
-  static constexpr int FLOATS = DB + 3 * C;
+  static constexpr int STP = DB + 3 * C;           // steep-block bits of each channel [32]
+  static constexpr int FLOATS = STP + 32;
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
 };
 static_assert(GradSmem::BYTES <= 227 * 1024, "grad_kernel shared memory");
+static_assert(4 * C * LDK <= 2 * 32 * VS, "pair sums alias the state slices");
 
 template <typename TIO, int KD>
 __global__ void __launch_bounds__(NTH, 1)
@@ -717,6 +767,7 @@ grad_kernel(const BwdParams p, const float* __restrict__ ws) {
   float* KB8 = sm + L::KB8;
   float* RED = sm + L::RED;
   float* DB = sm + L::DB;
+  unsigned* STP = reinterpret_cast<unsigned*>(sm + L::STP);
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int NC = num_chunks(p.T);
@@ -793,8 +844,8 @@ grad_kernel(const BwdParams p, const float* __restrict__ ws) {
         const float bt = t < p.T ? beta[(int64_t)t * p.b_s[1]] : 0.f;
         const float dl = j < i ? -al[0][nt][e] : 0.f;
         part[e >> 1] = fmaf(dl, lraw[i * C + j], part[e >> 1]);
-        LR[i * C + j] = bt * dl;
-        MQD[i * C + j] = j <= i ? am[0][nt][e] : 0.f;
+        LR[i * LDL + j] = bt * dl;
+        MQD[i * LDL + j] = j <= i ? am[0][nt][e] : 0.f;
       }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
@@ -846,11 +897,24 @@ grad_kernel(const BwdParams p, const float* __restrict__ ws) {
     cpa_wait<0>();
     __syncthreads();
     if (w == 0) {                                   // cumulative log decay of channel lane
-      float G = 0.f;
+      // and its steep blocks: block I (anchor a = 16 I) is steep when a factor
+      // exp(G_i - G_a) (i in I) or exp(G_a - G_j) (j < a + 16) leaves e^-80 .. e^80
+      float G = 0.f, runmin = 0.f, ga = 0.f, bmin = 0.f, bmax = 0.f;
+      unsigned bits = 0u;
       for (int i = 0; i < C; ++i) {
         G += GS[i * LDK + lane];
         GS[i * LDK + lane] = G;
+        if ((i & 15) == 0) {
+          ga = G;
+          bmin = bmax = G;
+        }
+        bmin = fminf(bmin, G);
+        bmax = fmaxf(bmax, G);
+        runmin = i == 0 ? G : fminf(runmin, G);
+        if ((i & 15) == 15 && (bmin - ga < -80.f || bmax - ga > 80.f || ga - runmin > 80.f))
+          bits |= 1u << (i >> 4);
       }
+      STP[lane] = bits;
     }
     // dEQ = dO S^T, dR S^T, dKbar = P dS_next^T: rows 16 (w % 4), channels 16 (w / 4) .. + 15
     {
@@ -878,34 +942,158 @@ grad_kernel(const BwdParams p, const float* __restrict__ ws) {
       RED[w * 32 + lane] = gcp;
     }
     __syncthreads();
-    // pair terms of dLraw and dMq, channel lane, rows i0 .. i0 + 7
-    float Gi[8], ki[8], qi[8], rowA[8], rowB[8], colA[8], colB[8];
+    // pair terms of dLraw and dMq by anchored 16-row blocks: for i in block I
+    // (anchor a = 16 I), exp(G_ic - G_jc) = exp(G_ic - G_ac) exp(G_ac - G_jc),
+    // both factors within e^-80 .. e^80 unless the block is steep for channel
+    // c (those pairs are left out here and added exactly below).  Warp w:
+    // block R = w % 4, channels cb .. cb + 15 (cb = 16 (w / 4)).
+    //   rowA_i = exp(G_i - G_aR) sum_j LR_ij k_j exp(G_aR - G_j),  rowB: MQD
+    //   colA_j = sum_{I >= R} exp(G_aI - G_j) sum_{i in I} LR_ij k_i exp(G_i - G_aI),
+    //   colB_j: MQD and q'
+    float* RA = SSs;                                // the state slices are dead here
+    float* RB = RA + C * LDK;
+    float* CA = RB + C * LDK;
+    float* CB = CA + C * LDK;
+    {
+      const int R = w & 3, cb = 16 * (w >> 2);
+      const int g = lane >> 2, tq = lane & 3;
+      float ra[1][2][4], rb[1][2][4];
+      zero(ra);
+      zero(rb);
+      for (int k = 0; k < 16 * (R + 1); k += 8) {
+        uint32_t lh[4], ll[4], mh[4], ml[4];
+        const float* la = LR + (16 * R + g) * LDL + k + tq;
+        const float* ma = MQD + (16 * R + g) * LDL + k + tq;
+        split3(la[0], lh[0], ll[0]);
+        split3(la[8 * LDL], lh[1], ll[1]);
+        split3(la[4], lh[2], ll[2]);
+        split3(la[8 * LDL + 4], lh[3], ll[3]);
+        split3(ma[0], mh[0], ml[0]);
+        split3(ma[8 * LDL], mh[1], ml[1]);
+        split3(ma[4], mh[2], ml[2]);
+        split3(ma[8 * LDL + 4], mh[3], ml[3]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int c = cb + 8 * nt + g;
+          const bool st = (STP[c] >> R) & 1u;
+          const float gaR = GS[16 * R * LDK + c];
+          const int j0 = k + tq, j1 = j0 + 4;
+          const float b0 = st ? 0.f : KS[j0 * LDK + c] * __expf(gaR - GS[j0 * LDK + c]);
+          const float b1 = st ? 0.f : KS[j1 * LDK + c] * __expf(gaR - GS[j1 * LDK + c]);
+          uint32_t bh[2], bl[2];
+          split3(b0, bh[0], bl[0]);
+          split3(b1, bh[1], bl[1]);
+          ptx::mma_tf32_16x8x8(ra[0][nt], ll, bh);
+          ptx::mma_tf32_16x8x8(ra[0][nt], lh, bl);
+          ptx::mma_tf32_16x8x8(ra[0][nt], lh, bh);
+          ptx::mma_tf32_16x8x8(rb[0][nt], ml, bh);
+          ptx::mma_tf32_16x8x8(rb[0][nt], mh, bl);
+          ptx::mma_tf32_16x8x8(rb[0][nt], mh, bh);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = acc_row(16 * R, lane, e), c = acc_col(cb, nt, lane, e);
+          const bool st = (STP[c] >> R) & 1u;
+          const float sc = st ? 0.f : __expf(GS[i * LDK + c] - GS[16 * R * LDK + c]);
+          RA[i * LDK + c] = ra[0][nt][e] * sc;
+          RB[i * LDK + c] = rb[0][nt][e] * sc;
+        }
+      float ca[1][2][4], cq[1][2][4];
+      zero(ca);
+      zero(cq);
+      for (int I = R; I < 4; ++I) {
+        float ta[1][2][4], tb[1][2][4];
+        zero(ta);
+        zero(tb);
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const int k = 16 * I + 8 * kk;
+          uint32_t lh[4], ll[4], mh[4], ml[4];      // A(j, i) = LR[i][j], rows j of block R
+          const float* la = LR + (k + tq) * LDL + 16 * R + g;
+          const float* ma = MQD + (k + tq) * LDL + 16 * R + g;
+          split3(la[0], lh[0], ll[0]);
+          split3(la[8], lh[1], ll[1]);
+          split3(la[4 * LDL], lh[2], ll[2]);
+          split3(la[4 * LDL + 8], lh[3], ll[3]);
+          split3(ma[0], mh[0], ml[0]);
+          split3(ma[8], mh[1], ml[1]);
+          split3(ma[4 * LDL], mh[2], ml[2]);
+          split3(ma[4 * LDL + 8], mh[3], ml[3]);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int c = cb + 8 * nt + g;
+            const bool st = (STP[c] >> I) & 1u;
+            const float gaI = GS[16 * I * LDK + c];
+            const int i0_ = k + tq, i1_ = i0_ + 4;
+            const float w0 = st ? 0.f : __expf(GS[i0_ * LDK + c] - gaI);
+            const float w1 = st ? 0.f : __expf(GS[i1_ * LDK + c] - gaI);
+            uint32_t bh[2], bl[2], qh[2], ql[2];
+            split3(KS[i0_ * LDK + c] * w0, bh[0], bl[0]);
+            split3(KS[i1_ * LDK + c] * w1, bh[1], bl[1]);
+            split3(QS[i0_ * LDK + c] * w0, qh[0], ql[0]);
+            split3(QS[i1_ * LDK + c] * w1, qh[1], ql[1]);
+            ptx::mma_tf32_16x8x8(ta[0][nt], ll, bh);
+            ptx::mma_tf32_16x8x8(ta[0][nt], lh, bl);
+            ptx::mma_tf32_16x8x8(ta[0][nt], lh, bh);
+            ptx::mma_tf32_16x8x8(tb[0][nt], ml, qh);
+            ptx::mma_tf32_16x8x8(tb[0][nt], mh, ql);
+            ptx::mma_tf32_16x8x8(tb[0][nt], mh, qh);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = acc_row(16 * R, lane, e), c = acc_col(cb, nt, lane, e);
+            const bool st = (STP[c] >> I) & 1u;
+            const float sc = st ? 0.f : __expf(GS[16 * I * LDK + c] - GS[j * LDK + c]);
+            ca[0][nt][e] = fmaf(ta[0][nt][e], sc, ca[0][nt][e]);
+            cq[0][nt][e] = fmaf(tb[0][nt][e], sc, cq[0][nt][e]);
+          }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = acc_row(16 * R, lane, e), c = acc_col(cb, nt, lane, e);
+          CA[j * LDK + c] = ca[0][nt][e];
+          CB[j * LDK + c] = cq[0][nt][e];
+        }
+    }
+    __syncthreads();
+    {                                               // steep blocks: exact pair terms
+      const unsigned stc = STP[lane];
+      for (int I = 0; I < 4 && stc != 0u; ++I) {
+        if (!((stc >> I) & 1u)) continue;
+#pragma unroll 1
+        for (int ii = 0; ii < 2; ++ii) {
+          const int i = 16 * I + 2 * w + ii;
+          const float Gi = GS[i * LDK + lane], ki = KS[i * LDK + lane], qi = QS[i * LDK + lane];
+          float sa = 0.f, sb = 0.f;
+          for (int j = 0; j <= i; ++j) {
+            const float D = __expf(Gi - GS[j * LDK + lane]);
+            const float l = LR[i * LDL + j] * D, m = MQD[i * LDL + j] * D;
+            const float kj = KS[j * LDK + lane];
+            sa = fmaf(l, kj, sa);
+            sb = fmaf(m, kj, sb);
+            atomicAdd(&CA[j * LDK + lane], l * ki);
+            atomicAdd(&CB[j * LDK + lane], m * qi);
+          }
+          RA[i * LDK + lane] += sa;
+          RB[i * LDK + lane] += sb;
+        }
+      }
+    }
+    __syncthreads();
+    float Gi[8], ki[8], qi[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       Gi[r] = GS[(i0 + r) * LDK + lane];
       ki[r] = KS[(i0 + r) * LDK + lane];
       qi[r] = QS[(i0 + r) * LDK + lane];
-      rowA[r] = rowB[r] = colA[r] = colB[r] = 0.f;
-    }
-    for (int j = 0; j < C; ++j) {
-      const float Gj = GS[j * LDK + lane], kj = KS[j * LDK + lane], qj = QS[j * LDK + lane];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const int i = i0 + r;
-        if (j < i) {
-          const float D = __expf(Gi[r] - Gj);
-          rowA[r] = fmaf(LR[i * C + j] * D, kj, rowA[r]);
-          rowB[r] = fmaf(MQD[i * C + j] * D, kj, rowB[r]);
-        } else if (j > i) {
-          const float D = __expf(Gj - Gi[r]);
-          colA[r] = fmaf(LR[j * C + i] * D, kj, colA[r]);
-          colB[r] = fmaf(MQD[j * C + i] * D, qj, colB[r]);
-        } else {
-          const float m = MQD[i * C + i];
-          rowB[r] = fmaf(m, kj, rowB[r]);
-          colB[r] = fmaf(m, qj, colB[r]);
-        }
-      }
     }
     // combine; dG replaces dEQ in E8, Kbar-column partial sums into RED[1]
     const float Gl = GS[(C - 1) * LDK + lane];
@@ -917,10 +1105,12 @@ grad_kernel(const BwdParams p, const float* __restrict__ ws) {
       const float kbar = ki[r] * eb;
       const float e8 = E8[i * LDK + lane], kb8 = KB8[i * LDK + lane];
       const float dkg = -bet[r] * KG8[i * LDK + lane];
-      const float dq = rowB[r] + e8 * gam;
-      const float dk = rowA[r] + colA[r] + colB[r] + dkg * gam + kb8 * eb;
-      const float dG = ki[r] * (rowA[r] - colA[r]) + qi[r] * rowB[r] - ki[r] * colB[r] +
-                       e8 * qi[r] * gam + dkg * ki[r] * gam - kb8 * kbar;
+      const float rA = RA[i * LDK + lane], rB = RB[i * LDK + lane];
+      const float cA = CA[i * LDK + lane], cB = CB[i * LDK + lane];
+      const float dq = rB + e8 * gam;
+      const float dk = rA + cA + cB + dkg * gam + kb8 * eb;
+      const float dG = ki[r] * (rA - cA) + qi[r] * rB - ki[r] * cB + e8 * qi[r] * gam +
+                       dkg * ki[r] * gam - kb8 * kbar;
       kbs = fmaf(kb8, kbar, kbs);
       E8[i * LDK + lane] = dG;
       if (t < p.T) {

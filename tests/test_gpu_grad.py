@@ -120,6 +120,38 @@ def test_backward_vs_oracle(case, cuda_dev):
         assert rel(got[n].float(), w) < tol, (n, rel(got[n].float(), w))
 
 
+def _steep_blocks_bwd(g, C=64):
+    """(b, h, chunk, 16-row block, channel) count whose decay inside the block,
+    g summed over its rows 2 .. 16, is below -80: the chunkwise backward leaves
+    those out of its anchored block GEMMs and adds their pair terms exactly."""
+    B, T, H, K = g.shape
+    Tp = -(-T // C) * C
+    x = torch.zeros(B, Tp, H, K, dtype=torch.float64, device=g.device)
+    x[:, :T] = g.double()
+    x = x.reshape(B, Tp // 16, 16, H, K)
+    return int((x[:, :, 1:].sum(2) < -80).sum()), x[:, :, 0].numel()
+
+
+@pytest.mark.parametrize("scale", [8.0, 20.0])
+def test_backward_steep_decay_blocks_vs_oracle(scale, cuda_dev):
+    kb = pkg()
+    x = kb.synth.make_inputs(1, 192, 2, 64, 32, dtype=torch.float32, seed=8, s0_std=0.02,
+                             device=cuda_dev)
+    x["g"] = x["g"] * scale
+    n_steep, total = _steep_blocks_bwd(x["g"])
+    assert 0 < n_steep < total, (n_steep, total)
+    gen = torch.Generator(device=cuda_dev).manual_seed(12)
+    do = torch.randn(1, 192, 2, 32, device=cuda_dev, generator=gen)
+    dS = torch.randn(1, 2, 64, 32, device=cuda_dev, generator=gen) * 0.1
+    got, _, _ = _run(kb, "chunk", x, x["S0"], None, 64, do, dS)
+    np_ = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
+    want = O.kda_backward(np_(x["q"]), np_(x["k"]), np_(x["v"]), np_(x["g"]), np_(x["beta"]),
+                          np_(x["S0"]), np_(do), np_(dS))
+    for n, w in zip(("dq", "dk", "dv", "dg", "dbeta", "dS0"), want):
+        assert torch.isfinite(got[n]).all(), n
+        assert rel(got[n].float(), w) < TOL_F32, (n, rel(got[n].float(), w))
+
+
 def test_chunkwise_and_recurrent_share_the_gradient(cuda_dev):
     """Both functions are one function: the same backward through either."""
     kb = pkg()

@@ -25,9 +25,12 @@
 //
 // Four kernels, fp32 data; every GEMM runs on the tensor cores as 3xTF32
 // (x = hi + lo, both exact in tf32; hi*hi + hi*lo + lo*hi, ~fp32 accuracy):
-//  * prep_kernel  (b, h, chunk): the pair sums Lraw and Mq (one exponential
-//    per pair and channel, no Gam ratios that could overflow), Tinv by forward
-//    substitution, KG, Kbar, EQ, GamC -- written to the per-chunk record;
+//  * prep_kernel  (b, h, chunk): the pair sums Lraw and Mq as anchored 16-row
+//    block GEMMs (exp(G_ic - G_jc) = exp(G_ic - G_ac) exp(G_ac - G_jc) with the
+//    anchor a at the start of i's block, each factor within e^-80 .. e^80;
+//    channels for which a block is steeper add their exact pair terms
+//    separately), Tinv by forward substitution, KG, Kbar, EQ, GamC -- written
+//    to the per-chunk record;
 //  * fchain_kernel (b, h, 32 state columns): S chunk by chunk (X = KG S,
 //    P = Tinv R, S_next = GamC S + Kbar^T P), storing every chunk-start state
 //    and the chunk's P and Z;
@@ -35,8 +38,8 @@
 //    gradient of every chunk-end state and dR, writing dv; it needs no S, so
 //    it runs beside fchain on a second stream;
 //  * grad_kernel  (b, h, chunk): dL, dMq, dEQ, dKG, dKbar from the stored
-//    P, dR, states and dO, the pair terms, and dq, dk, dg, dbeta (final sums,
-//    no partials over V).
+//    P, dR, states and dO, the pair terms (the same anchored block GEMMs), and
+//    dq, dk, dg, dbeta (final sums, no partials over V).
 // The GEMMs are warp tiles of mma.sync m16n8k8 over operands in shared memory
 // read through (row, k) strides, so no operand needs a transposed copy; row
 // strides are padded so that the fragment loads are free of bank conflicts.

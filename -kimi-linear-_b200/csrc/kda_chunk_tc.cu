@@ -158,6 +158,9 @@ static_assert(PREP_SMEM <= 227 * 1024, "prep shared memory");
 // where it is read later); M (fp32, pitch LMP) reuses the k*ra array and the
 // inversion scratch the q*ra array once the Gram is done.
 constexpr int PREP_THREADS = 512;
+// the prep thread that issues the bulk stores of the chunk images and
+// publishes them (warp 14: idle in the phase during which it publishes)
+constexpr int PUB = 448;
 
 // 3xTF32 split: x ~= hi + lo with both parts exact in tf32
 __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
@@ -279,15 +282,18 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   const int total = NT * BH;                          // < 2^31 (checked on the host)
   const int stride = gridDim.x;
   int chunk = blockIdx.x;
-  // image whose ready flag thread 0 still owes (set once its bulk stores
-  // completed; with `newest` the most recently committed store may still run)
+  // image whose ready flag thread PUB still owes (set once its bulk stores
+  // completed; with `newest` the most recently committed store may still run).
+  // PUB issued those stores, so it alone can wait for them; the async-proxy
+  // fence orders them before the release, and the release (gpu scope) orders
+  // every other thread's stores of the image, which precede it through a CTA
+  // barrier.
   long pend = -1;
   auto publish = [&](bool newest) {
     if (pend >= 0) {
       if (newest) ptx::bulk_wait_le<1>();
       else ptx::bulk_wait_all();
       ptx::fence_proxy_async_global();
-      __threadfence();
       ptx::st_release_gpu(flags + pend, 1u);
       pend = -1;
     }
@@ -465,7 +471,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   if (tid < CH) sbeta[tid] = beta_c;
   // the image staging region is written from here on: the previous chunk's
   // bulk stores must have read it
-  if (tid == 0) ptx::bulk_wait_read();
+  if (tid == PUB) ptx::bulk_wait_read();
   __syncthreads();
   {
     float Zx[4], Zy[4], eZx[4], eZy[4];
@@ -554,7 +560,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   }
   ptx::fence_proxy_async_smem();
   __syncthreads();
-  if (tid == 0) {              // Kbar^T and d are final: [IMG_A3, IMG_SHARED) leaves now
+  if (tid == PUB) {            // Kbar^T and d are final: [IMG_A3, IMG_SHARED) leaves now
     ptx::bulk_s2g(ws + img_off + IMG_A3, img + IMG_A3, IMG_SHARED - IMG_A3);
     ptx::bulk_commit();
   }
@@ -669,9 +675,6 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     }
     }
   }
-  // the previous chunk's U^T / F^T store has had phases 1-2 to complete:
-  // publish that image (this chunk's Kbar^T / d store, the newest, may run on)
-  if (tid == 0) publish(true);
   __syncthreads();
 
   // ---- 3. M = (I + L)^-1 Diag(beta): blocked forward substitution ----------
@@ -701,27 +704,81 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     }
   }
   __syncthreads();
-  // off-diagonal blocks M_rj = -D_r sum_{t=j}^{r-1} L_rt M_tj, by distance r - j;
-  // a warp pair per block, one 8-column n-tile each (the products are
-  // column-separable)
-  for (int dist = 1; dist <= 3; ++dist) {
-    if (warp < 2 * (4 - dist)) {
-      const int j = warp >> 1, nt = warp & 1, rb = j + dist;
-      float tacc[4] = {0.f, 0.f, 0.f, 0.f};
-      const float* La = Lm + (16 * rb) * LMP + 16 * j;
-      const float* Mb = Mm + (16 * j) * LMP + 16 * j + 8 * nt;
-      if (dist == 1) gemm16x8_3xtf32<2>(tacc, La, LMP, Mb, LMP, lane);
-      else if (dist == 2) gemm16x8_3xtf32<4>(tacc, La, LMP, Mb, LMP, lane);
-      else gemm16x8_3xtf32<6>(tacc, La, LMP, Mb, LMP, lane);
-      float* Tw = Ts + warp * (16 * TSP);
+  // the previous chunk's image is complete once its bulk stores are: PUB
+  // publishes it while warps 0-11 run the first doubling level (its release
+  // waits for the stores; this chunk's Kbar^T / d store, the newest, may run on)
+  if (tid == PUB) publish(true);
+  // off-diagonal blocks by recursive doubling, D_r = M_rr: the 32 x 32 halves
+  // first (M10 = -D1 L10 D0, M32 = -D3 L32 D2), then the lower-left quarter
+  // X = -[D2 0; M32 D3] [L20 L21; L30 L31] [D0 0; M10 D1].  Two levels instead
+  // of three (by distance r - j), the products that need only the diagonal
+  // blocks in the first.  A warp owns one 8-column n-tile of a block (the
+  // products are column-separable); T / Y tiles go through shared memory.
+  {
+    float* Tw = Ts + warp * (16 * TSP);            // per-warp 16 x 16 scratch
+    float* Ys = Ts + 16 * (16 * TSP);              // Y[r - 2][j], 16 x TSP each
+    auto blk = [&](int r, int j) { return Mm + (16 * r) * LMP + 16 * j; };
+    auto lblk = [&](int r, int j) { return Lm + (16 * r) * LMP + 16 * j; };
+    auto yblk = [&](int r, int j) { return Ys + ((r - 2) * 2 + j) * (16 * TSP); };
+    // fragment <-> 16 x 8 tile at column offset c0 of a pitch-TSP array
+    auto st_frag = [&](float* dst, int c0, const float* acc) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) Tw[(gid + 8 * (e >> 1)) * TSP + 2 * tig + (e & 1)] = tacc[e];
-      __syncwarp();
-      float macc[4] = {0.f, 0.f, 0.f, 0.f};
-      gemm16x8_3xtf32<2>(macc, Mm + (16 * rb) * LMP + 16 * rb, LMP, Tw, TSP, lane);
+      for (int e = 0; e < 4; ++e) dst[(gid + 8 * (e >> 1)) * TSP + c0 + 2 * tig + (e & 1)] = acc[e];
+    };
+    auto ld_frag = [&](const float* src, int c0, float* acc) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = src[(gid + 8 * (e >> 1)) * TSP + c0 + 2 * tig + (e & 1)];
+    };
+    auto st_m = [&](int r, int j, int nt, const float* acc) {
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        Mm[(16 * rb + gid + 8 * (e >> 1)) * LMP + 16 * j + 8 * nt + 2 * tig + (e & 1)] = -macc[e];
+        Mm[(16 * r + gid + 8 * (e >> 1)) * LMP + 16 * j + 8 * nt + 2 * tig + (e & 1)] = -acc[e];
+    };
+    if (warp < 12) {                               // level 1
+      const int nt = warp & 1;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (warp < 4) {                              // M10 (warps 0-1), M32 (warps 2-3)
+        const int r = warp < 2 ? 1 : 3, j = r - 1;
+        gemm16x8_3xtf32<2>(acc, lblk(r, j), LMP, blk(j, j) + 8 * nt, LMP, lane);
+        st_frag(Tw, 0, acc);
+        __syncwarp();
+        float macc[4] = {0.f, 0.f, 0.f, 0.f};
+        gemm16x8_3xtf32<2>(macc, blk(r, r), LMP, Tw, TSP, lane);
+        st_m(r, j, nt, macc);
+      } else {                                     // Y21, Y31 = L_r1 D1; Y20', Y30' = L_r0 D0
+        const int j = warp < 8 ? 1 : 0, r = 2 + ((warp >> 1) & 1);
+        gemm16x8_3xtf32<2>(acc, lblk(r, j), LMP, blk(j, j) + 8 * nt, LMP, lane);
+        st_frag(yblk(r, j), 8 * nt, acc);
+      }
+    }
+    __syncthreads();
+    if (warp < 8) {                                // level 2: blocks (r, j), r in {2, 3}
+      const int r = 2 + (warp >> 2), j = (warp >> 1) & 1, nt = warp & 1;
+      float macc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (j == 0) {                                // Y20 = Y20' + L21 M10 (and Y30 for r = 3)
+        float y[4];
+        ld_frag(yblk(2, 0), 8 * nt, y);
+        gemm16x8_3xtf32<2>(y, lblk(2, 1), LMP, blk(1, 0) + 8 * nt, LMP, lane);
+        st_frag(Tw, 0, y);
+        if (r == 3) {
+          ld_frag(yblk(3, 0), 8 * nt, y);
+          gemm16x8_3xtf32<2>(y, lblk(3, 1), LMP, blk(1, 0) + 8 * nt, LMP, lane);
+          st_frag(Tw, 8, y);
+        }
+        __syncwarp();
+        if (r == 2) {                              // M20 = -D2 Y20
+          gemm16x8_3xtf32<2>(macc, blk(2, 2), LMP, Tw, TSP, lane);
+        } else {                                   // M30 = -(M32 Y20 + D3 Y30)
+          gemm16x8_3xtf32<2>(macc, blk(3, 2), LMP, Tw, TSP, lane);
+          gemm16x8_3xtf32<2>(macc, blk(3, 3), LMP, Tw + 8, TSP, lane);
+        }
+      } else if (r == 2) {                         // M21 = -D2 Y21
+        gemm16x8_3xtf32<2>(macc, blk(2, 2), LMP, yblk(2, 1) + 8 * nt, TSP, lane);
+      } else {                                     // M31 = -(M32 Y21 + D3 Y31)
+        gemm16x8_3xtf32<2>(macc, blk(3, 2), LMP, yblk(2, 1) + 8 * nt, TSP, lane);
+        gemm16x8_3xtf32<2>(macc, blk(3, 3), LMP, yblk(3, 1) + 8 * nt, TSP, lane);
+      }
+      st_m(r, j, nt, macc);
     }
     __syncthreads();
   }
@@ -791,7 +848,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   const bool mma_ok = ptx::mbar_wait(mbar, it & 1u, kWaitNs);
   ptx::tc_fence_after();
   if (__syncthreads_or(!mma_ok)) {                       // the GEMM never finished: give up
-    if (tid == 0) {
+    if (tid == PUB) {
       atomicExch(&g_kda_device_error, 2);
       ptx::mbar_wait(mbar, it & 1u, kWaitNs / 2);
       ptx::bulk_wait_read();
@@ -856,11 +913,11 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   }
   // end of the chunk: TMEM read out, U^T / F^T staged; they leave with one bulk
   // store, and the image is published (ready flag) once all its stores are
-  // complete -- by thread 0 during the next chunk, or right after the loop
+  // complete -- by thread PUB during the next chunk, or right after the loop
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_before();
   __syncthreads();
-  if (tid == 0) {
+  if (tid == PUB) {
     ptx::bulk_s2g(ws + img_off + IMG_U, img + IMG_U, IMG_BYTES - IMG_U);
     ptx::bulk_commit();
     pend = (long)(img_off / IMG_BYTES);
@@ -871,7 +928,7 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
   ptx::tc_fence_after();
   }  // chunk loop
 
-  if (tid == 0) publish(false);
+  if (tid == PUB) publish(false);
   if (warp == 0) {
     ptx::tmem_dealloc(*tslot, kPrepTmemCols);
   }
@@ -899,27 +956,31 @@ __device__ __forceinline__ void add8_f16(float* x, int4 v) {
 //   P16^T = f16(U^T + D1)             -> TMEM, A operand of D3
 //   D3 = P16^T Kbar       [128 x 128] = (Kbar^T P)^T
 //   S^T <- S^T Diag(d) + D3           fp32 master state, in registers
-//   D2 = S16^T E^T        [128 x 64]  = O^T - F^T       (O = E S + F)
+//   O^T = S16^T E^T + F^T [128 x 64]                    (O = E S + F)
 // S16^T is the f16 copy of S both GEMMs use, as the reference rounds S to its
 // transient dtype for them (kda.py:176).  A operands come from TMEM (no shared
 // memory round trip of S or P); B operands are the chunk image in shared memory.
 // Warp roles:
-//  * chain warps 0-7: warp w owns TMEM lanes 32 (w % 4).. (value columns
+//  * chain warps 0-7: warp w owns TMEM lanes 32 (w % 4) .. +31 (value columns
 //    v = 32 (w % 4) + lane) and half w / 4 of every product's columns; thread
-//    (v, half) keeps S^T[v, 64 half .. 64 half + 63] in registers.  Warp 0
-//    issues the MMAs.  Per chunk: f16 copy of S -> D1 -> P -> D3 -> S update.
-//  * output warps 8-11: O = F + D2 of each chunk (D2 double-buffered in TMEM),
-//    transposed through a shared-memory tile into 16-byte global stores, off
-//    the chain's critical path.
-//  * producer warp 12: waits for each image's ready flag (set by the prep grid,
+//    (v, half) keeps S^T[v, 64 half .. 64 half + 63] in registers.  Per chunk:
+//    P hand-off after D1, then the state update after D3, which writes the
+//    next chunk's f16 copy of S into the other TMEM buffer.
+//  * output warps 8-11: O = F + D2 of each chunk (O double-buffered in TMEM),
+//    transposed through a shared-memory tile into 16-byte global stores.
+//  * MMA warp 12: one thread issues every GEMM: D1 as soon as S16 is in
+//    TMEM, D3 as soon as P16 is, then the chunk's output GEMM, which the
+//    tensor pipe runs while the chain warps update the state.
+//  * producer warp 13: waits for each image's ready flag (set by the prep grid,
 //    which may still be running) and copies the parts the chain needs
-//    (-W, Kbar^T, d, U^T: three stages) and the parts the output warps need
-//    (E, F^T: two stages) into shared memory.
+//    (-W, Kbar^T, d, U^T: three stages) and the parts the output GEMM and its
+//    warps need (E, F^T: two stages) into shared memory.
 // Every wait is bounded; on expiry the CTA sets the device error word, lets its
-// copies in flight land, frees TMEM and returns.
+// copies and MMAs in flight finish, frees TMEM and returns.
 constexpr int ST_CHAIN_WARPS = 8, ST_OUT_WARPS = 4;
-constexpr int ST_WARPS = ST_CHAIN_WARPS + ST_OUT_WARPS + 1;
-constexpr int ST_CHAIN = ST_CHAIN_WARPS * 32;    // threads of the chain warps
+constexpr int ST_MMA_WARP = ST_CHAIN_WARPS + ST_OUT_WARPS;
+constexpr int ST_PROD_WARP = ST_MMA_WARP + 1;
+constexpr int ST_WARPS = ST_PROD_WARP + 1;
 // chain stage: -W [64 x 128] | Kbar^T [128 x 64] | d | U^T
 constexpr int CS_W = 0, CS_A3 = 16384, CS_D = 32768, CS_U = 33280, CS_BYTES = 49664;
 // output stage: E [64 x 128] | F^T
@@ -928,17 +989,17 @@ constexpr int ST_NCS = 3, ST_NOS = 2;             // stages per ring
 constexpr int ST_OS0 = ST_NCS * CS_BYTES;
 constexpr int ST_OT = ST_OS0 + ST_NOS * OS_BYTES;  // output tile O [64][128] (I/O dtype)
 constexpr int ST_BAR = ST_OT + CH * KD * 2;
-constexpr int ST_SMEM = ST_BAR + 160;
+constexpr int ST_SMEM = ST_BAR + 192;
 static_assert(ST_SMEM <= 227 * 1024, "state shared memory");
 static_assert(CS_D - CS_A3 == IMG_D - IMG_A3 && CS_U - CS_A3 == IMG_U - IMG_A3 &&
                   CS_BYTES - CS_A3 == IMG_F - IMG_A3, "chain stage layout");
 // prep (231 KB) and state CTAs can never share an SM, so TMEM allocations of
 // the two grids never contend
 static_assert(ST_SMEM + PREP_SMEM > 228 * 1024, "prep and state CTAs must not share an SM");
-// TMEM columns: D1 fp32 [128 x 64]; D2 fp32 [128 x 64] twice (by chunk parity);
-// D3 fp32 [128 x 128]; two f16 copies of S^T (A operands, 128 keys = 64
+// TMEM columns: D1 fp32 [128 x 64]; D3 fp32 [128 x 128]; O fp32 [128 x 64]
+// twice (by chunk parity); two f16 copies of S^T (A operands, 128 keys = 64
 // columns each, by chunk parity); P16^T (64 chunk rows = 32 columns)
-constexpr uint32_t TC_D1 = 0, TC_D2A = 64, TC_D3 = 128, TC_AS = 256, TC_AP = 384, TC_D2B = 448;
+constexpr uint32_t TC_D1 = 0, TC_D3 = 64, TC_O = 192, TC_S = 320, TC_P = 448;
 constexpr uint32_t ST_TMEM_COLS = 512;
 
 // bounded mbarrier wait that also gives up as soon as the CTA is aborting
@@ -976,15 +1037,19 @@ __global__ void __launch_bounds__(ST_WARPS * 32, 1)
 state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
              const unsigned int* __restrict__ flags) {
   extern __shared__ __align__(1024) uint8_t sm[];
-  uint64_t* cfull = reinterpret_cast<uint64_t*>(sm + ST_BAR);  // [3] chain part landed
-  uint64_t* cempty = cfull + 3;                                 // [3] chain part consumed (8 warps)
-  uint64_t* ofull = cfull + 6;                                  // [2] output part landed
-  uint64_t* oempty = cfull + 8;                                 // [2] output part consumed (4 warps)
-  uint64_t* bd1 = cfull + 10;                                   // D1 done
-  uint64_t* bd3 = cfull + 11;                                   // D3 done
-  uint64_t* bd2 = cfull + 12;                                   // [2] D2 done, by chunk parity
-  uint64_t* d2free = cfull + 14;                                // [2] D2 read out (4 warps)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(cfull + 16);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + ST_BAR);
+  uint64_t* cfull = bars;          // [3] chain part landed (producer, bytes)
+  uint64_t* cempty = bars + 3;     // [3] chain part consumed (8 chain warps)
+  uint64_t* ofull = bars + 6;      // [2] output part landed
+  uint64_t* oempty = bars + 8;     // [2] output part consumed (4 output warps)
+  uint64_t* odone = bars + 10;     // [2] output GEMM complete (MMA commit)
+  uint64_t* ofree = bars + 12;     // [2] O buffer read out (4 output warps)
+  uint64_t* d1full = bars + 14;    // D1 complete
+  uint64_t* d3full = bars + 15;    // D3 complete
+  uint64_t* sready = bars + 16;    // S16 written to TMEM (8 chain warps)
+  uint64_t* pready = bars + 17;    // P16 written to TMEM (8 chain warps)
+  uint64_t* mfin = bars + 18;      // every MMA issued has completed (teardown)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1006,11 +1071,14 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
     for (int s = 0; s < ST_NOS; ++s) {
       ptx::mbar_init(&ofull[s], 1);
       ptx::mbar_init(&oempty[s], ST_OUT_WARPS);
-      ptx::mbar_init(&bd2[s], 1);
-      ptx::mbar_init(&d2free[s], ST_OUT_WARPS);
+      ptx::mbar_init(&odone[s], 1);
+      ptx::mbar_init(&ofree[s], ST_OUT_WARPS);
     }
-    ptx::mbar_init(bd1, 1);
-    ptx::mbar_init(bd3, 1);
+    ptx::mbar_init(d1full, 1);
+    ptx::mbar_init(d3full, 1);
+    ptx::mbar_init(sready, ST_CHAIN_WARPS);
+    ptx::mbar_init(pready, ST_CHAIN_WARPS);
+    ptx::mbar_init(mfin, 1);
     ptx::fence_mbar_init();
     *abort_flag = 0;
   }
@@ -1019,7 +1087,7 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
   ptx::tc_fence_after();
   const uint32_t tbase = *tslot;
 
-  if (warp == ST_WARPS - 1) {
+  if (warp == ST_PROD_WARP) {
     // ---- producer: ready flag -> bulk copies of the chain and output parts --
     if (lane == 0) {
       int clast[ST_NCS] = {-1, -1, -1}, olast[ST_NOS] = {-1, -1};
@@ -1054,6 +1122,56 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
       for (int s = 0; s < ST_NOS; ++s)
         if (olast[s] >= 0) ptx::mbar_wait(&ofull[s], (olast[s] >> 1) & 1, kWaitNs / 2);
     }
+  } else if (warp == ST_MMA_WARP) {
+    // ---- MMA issue (one thread) ---------------------------------------------
+    if (lane == 0) {
+      const uint32_t sm0 = ptx::smem_u32(sm);
+      constexpr uint32_t ID64 = ptx::idesc_f16_f32(128, 64, false, false);
+      constexpr uint32_t ID128 = ptx::idesc_f16_f32(128, 128, false, false);
+      bool ok = true;
+      for (int n = 0; n < NT && ok; ++n) {
+        const int cs = n % ST_NCS, os = n & 1;
+        const uint32_t as = tbase + TC_S + 64 * (n & 1);
+        // D1 = S16^T (-W)^T: S16(n) in TMEM, image n's chain part landed
+        ok = mbar_wait_or_abort(sready, n & 1, abort_flag) &&
+             mbar_wait_or_abort(&cfull[cs], (n / ST_NCS) & 1, abort_flag);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint64_t bw = ptx::sdesc(sm0 + cs * CS_BYTES + CS_W, 128, 2048);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          ptx::mma_f16_ts(tbase + TC_D1, as + 8 * ks, bw + 16 * ks, ID64, ks > 0);
+        ptx::tc_commit(d1full);
+        // D3 = P16^T Kbar once the chain warps wrote P16(n)
+        ok = mbar_wait_or_abort(pready, n & 1, abort_flag);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint64_t bk = ptx::sdesc(sm0 + cs * CS_BYTES + CS_A3, 128, 1024);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          ptx::mma_f16_ts(tbase + TC_D3, tbase + TC_P + 8 * ks, bk + 16 * ks, ID128, ks > 0);
+        ptx::tc_commit(d3full);
+        // O(n) = S16^T(n) E^T into O buffer n & 1 (the output warps read O(n - 2)
+        // out of it); the tensor pipe runs it during the state update
+        ok = mbar_wait_or_abort(&ofull[os], (n >> 1) & 1, abort_flag);
+        if (ok && n >= ST_NOS) ok = mbar_wait_or_abort(&ofree[os], ((n >> 1) - 1) & 1, abort_flag);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint64_t be = ptx::sdesc(sm0 + ST_OS0 + os * OS_BYTES + OS_E, 128, 2048);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          ptx::mma_f16_ts(tbase + TC_O + 64 * os, as + 8 * ks, be + 16 * ks, ID64, ks > 0);
+        ptx::tc_commit(&odone[os]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicExch(&g_kda_device_error, 1);
+      }
+      // nothing may still run on TMEM when it is released
+      ptx::tc_commit(mfin);
+      ptx::mbar_wait(mfin, 0, kWaitNs / 2);
+    }
+    __syncwarp();
   } else if (warp >= ST_CHAIN_WARPS) {
     // ---- output warps: O = F + D2, one value column per thread -------------
     const int v = 32 * (warp - ST_CHAIN_WARPS) + lane;
@@ -1063,28 +1181,31 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
     const bool ovec = (reinterpret_cast<uintptr_t>(p.o) % 16) == 0 && p.o_s[0] % 8 == 0 &&
                       p.o_s[1] % 8 == 0 && p.o_s[2] % 8 == 0;
     TIO* otile = reinterpret_cast<TIO*>(sm + ST_OT);
-    const int ot = tid - ST_CHAIN;                 // 0 .. 127
+    const int ot = tid - ST_CHAIN_WARPS * 32;      // 0 .. 127
 #pragma unroll 1
     for (int m = 0; m < NT; ++m) {
       const int os = m & 1;
-      if (!mbar_wait_or_abort(&bd2[os], (m >> 1) & 1, abort_flag)) break;
+      // the four warps agree, so none is left alone at the tile barriers below
+      const bool ok = mbar_wait_or_abort(&odone[os], (m >> 1) & 1, abort_flag) &&
+                      mbar_wait_or_abort(&ofull[os], (m >> 1) & 1, abort_flag);
+      if (ptx::bar_red_or(2, ST_OUT_WARPS * 32, !ok)) break;
       ptx::tc_fence_after();
       float o[64];
-      ptx::tmem_ld<32>(tl + (os ? TC_D2B : TC_D2A), o);
-      ptx::tmem_ld<32>(tl + (os ? TC_D2B : TC_D2A) + 32, o + 32);
+      ptx::tmem_ld<32>(tl + TC_O + 64 * os, o);
+      ptx::tmem_ld<32>(tl + TC_O + 64 * os + 32, o + 32);
       ptx::tmem_wait_ld();
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&d2free[os]);       // D2 buffer may be rewritten
+      if (lane == 0) ptx::mbar_arrive(&ofree[os]);       // O buffer may be rewritten
       const uint8_t* frow = sm + ST_OS0 + os * OS_BYTES + OS_F + v * 128;
 #pragma unroll
       for (int i = 0; i < 8; ++i) add8_f16(o + 8 * i, *trow_chunk(frow, i, v));
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&oempty[os]);       // E (read by D2) and F consumed
-      bar_named(2, ST_OUT_WARPS * 32);                     // previous tile stored
+      if (lane == 0) ptx::mbar_arrive(&oempty[os]);      // E (read by O(m)) and F consumed
+      bar_named(2, ST_OUT_WARPS * 32);                    // previous tile stored
 #pragma unroll
       for (int c = 0; c < CH; ++c) st(otile + c * KD + v, o[c]);
-      bar_named(2, ST_OUT_WARPS * 32);                     // tile complete
+      bar_named(2, ST_OUT_WARPS * 32);                    // tile complete
       // 64 rows x 256 bytes = 1024 vectors of 16 bytes over 128 threads
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -1106,9 +1227,6 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
     const int wq = warp & 3, hh = warp >> 2;
     const int v = 32 * wq + lane;                  // value column = TMEM lane
     const uint32_t tl = tbase + (static_cast<uint32_t>(32 * wq) << 16);
-    const uint32_t sm0 = ptx::smem_u32(sm);
-    constexpr uint32_t ID64 = ptx::idesc_f16_f32(128, 64, false, false);
-    constexpr uint32_t ID128 = ptx::idesc_f16_f32(128, 128, false, false);
 
     float S[64];                                   // S^T[v, 64 hh + j]
     if (p.state_in != nullptr) {
@@ -1119,26 +1237,8 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
 #pragma unroll
       for (int j = 0; j < 64; ++j) S[j] = 0.f;
     }
-    bool bad = false, failed = false;
-    // D2(j) = S16^T(j) E_j^T into D2 buffer j & 1 (warp 0): E_j landed, and the
-    // output warps read D2(j - 2) out of that buffer
-    auto issue_d2 = [&](int j) -> bool {
-      const int jb = j & 1;
-      bool ok = mbar_wait_or_abort(&ofull[jb], (j >> 1) & 1, abort_flag);
-      if (j >= 2) ok = ok && mbar_wait_or_abort(&d2free[jb], ((j >> 1) - 1) & 1, abort_flag);
-      ptx::tc_fence_after();
-      if (ok && ptx::elect_one()) {
-        const uint64_t be = ptx::sdesc(sm0 + ST_OS0 + jb * OS_BYTES + OS_E, 128, 2048);
-        const uint32_t d2 = tbase + (jb ? TC_D2B : TC_D2A);
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          ptx::mma_f16_ts(d2, tbase + TC_AS + 64 * jb + 8 * ks, be + 16 * ks, ID64, ks > 0);
-        ptx::tc_commit(&bd2[jb]);
-      }
-      __syncwarp();
-      return ok;
-    };
-    // f16 copy of S^T (A operand of D1, D2) into TMEM buffer `col`, 16 keys at a time
+    // f16 copy of S^T (A operand of D1 and the output GEMM) into TMEM buffer
+    // `col`, 16 keys at a time
     auto store_s16 = [&](uint32_t col, int q) {
       uint32_t pk[8];
 #pragma unroll
@@ -1150,42 +1250,32 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
           "r"(pk[7])
           : "memory");
     };
+    // every arrival of a warp comes after its TMEM stores completed
+    auto signal = [&](uint64_t* bar) {
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar);
+    };
 #pragma unroll
-    for (int q = 0; q < 4; ++q) store_s16(TC_AS, q);
-    ptx::tmem_wait_st();
+    for (int q = 0; q < 4; ++q) store_s16(TC_S, q);
+    signal(sready);
+    bool ok = true;
 #pragma unroll 1
     for (int n = 0; n < NT; ++n) {
-      const int cs = n % ST_NCS, os = n & 1;
+      const int cs = n % ST_NCS;
       const uint8_t* cst = sm + cs * CS_BYTES;
-      const uint32_t as_col = TC_AS + 64 * (n & 1);
-      // (a) the f16 copy of S^T(n) is in TMEM (written with the previous
-      // chunk's state update); image n's chain part must have landed
-      ptx::tc_fence_before();
-      bad |= !mbar_wait_or_abort(&cfull[cs], (n / ST_NCS) & 1, abort_flag);
-      if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
-      if (warp == 0) {                             // D1 = S16^T (-W)^T, then D2(n - 1)
-        ptx::tc_fence_after();
-        if (ptx::elect_one()) {
-          const uint64_t bw = ptx::sdesc(sm0 + cs * CS_BYTES + CS_W, 128, 2048);
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            ptx::mma_f16_ts(tbase + TC_D1, tbase + as_col + 8 * ks, bw + 16 * ks, ID64, ks > 0);
-          ptx::tc_commit(bd1);
-        }
-        __syncwarp();
-        // the previous chunk's output GEMM goes in behind D1, so the tensor
-        // pipe runs it during the P hand-off instead of between D3 and the
-        // next D1 (its waits are off the chain: D1 is already issued)
-        if (n >= 1) bad |= !issue_d2(n - 1);
-      }
-      // (b) P^T = U^T + D1 -> f16 -> TMEM; U^T is read while D1 runs
+      // (a) P^T = U^T + D1 -> f16 -> TMEM; U^T is read while D1 runs
+      ok = mbar_wait_or_abort(&cfull[cs], (n / ST_NCS) & 1, abort_flag);
+      if (!ok) break;
       int4 ur[4];
       {
         const uint8_t* urow = cst + CS_U + v * 128;
 #pragma unroll
         for (int i = 0; i < 4; ++i) ur[i] = *trow_chunk(urow, 4 * hh + i, v);
       }
-      bad |= !mbar_wait_or_abort(bd1, n & 1, abort_flag);
+      ok = mbar_wait_or_abort(d1full, n & 1, abort_flag);
+      if (!ok) break;
       ptx::tc_fence_after();
       {
         float x[32];
@@ -1196,55 +1286,41 @@ state_kernel(const ChunkParams p, const uint8_t* __restrict__ ws,
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) pk[i] = pack_h2(x[2 * i], x[2 * i + 1]);
-        ptx::tmem_st<16>(tl + TC_AP + 16 * hh, reinterpret_cast<const float*>(pk));
-        ptx::tmem_wait_st();
+        ptx::tmem_st<16>(tl + TC_P + 16 * hh, reinterpret_cast<const float*>(pk));
       }
-      ptx::tc_fence_before();
-      if (ptx::bar_red_or(1, ST_CHAIN, bad)) { failed = true; break; }
-      if (warp == 0) {                             // D3 = P16^T Kbar
-        ptx::tc_fence_after();
-        if (ptx::elect_one()) {
-          const uint64_t bk = ptx::sdesc(sm0 + cs * CS_BYTES + CS_A3, 128, 1024);
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            ptx::mma_f16_ts(tbase + TC_D3, tbase + TC_AP + 8 * ks, bk + 16 * ks, ID128, ks > 0);
-          ptx::tc_commit(bd3);
-        }
-        __syncwarp();
-      }
-      // (c) S^T <- S^T Diag(d) + D3, and its f16 copy for chunk n + 1 into the
-      // other TMEM buffer, last read by D1 / D2 of chunk n - 1 (D2 the later)
-      const float* dk = reinterpret_cast<const float*>(cst + CS_D) + 64 * hh;
-      if (n >= 1) bad |= !mbar_wait_or_abort(&bd2[os ^ 1], ((n - 1) >> 1) & 1, abort_flag);
-      bad |= !mbar_wait_or_abort(bd3, n & 1, abort_flag);
+      signal(pready);
+      // (b) S^T <- S^T Diag(d) + D3, and its f16 copy for chunk n + 1 into the
+      // other TMEM buffer (last read by D1(n - 1) and O(n - 1), which completed
+      // before D1(n))
+      ok = mbar_wait_or_abort(d3full, n & 1, abort_flag);
+      if (!ok) break;
       ptx::tc_fence_after();
-      const uint32_t as_next = TC_AS + 64 * ((n + 1) & 1);
+      const float* dk = reinterpret_cast<const float*>(cst + CS_D) + 64 * hh;
+      const uint32_t snext = TC_S + 64 * ((n + 1) & 1);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float dq[16], x[16];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 t = reinterpret_cast<const float4*>(dk + 16 * q)[i];
-          dq[4 * i] = t.x; dq[4 * i + 1] = t.y; dq[4 * i + 2] = t.z; dq[4 * i + 3] = t.w;
-        }
-        ptx::tmem_ld16(tl + TC_D3 + 64 * hh + 16 * q, x);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float x[32];
+        ptx::tmem_ld<32>(tl + TC_D3 + 64 * hh + 32 * h2, x);
         ptx::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) S[16 * q + j] = fmaf(S[16 * q + j], dq[j], x[j]);
-        store_s16(as_next, q);
+        for (int i = 0; i < 8; ++i) {
+          const float4 t = reinterpret_cast<const float4*>(dk + 32 * h2)[i];
+          float* sp = S + 32 * h2 + 4 * i;
+          sp[0] = fmaf(sp[0], t.x, x[4 * i]);
+          sp[1] = fmaf(sp[1], t.y, x[4 * i + 1]);
+          sp[2] = fmaf(sp[2], t.z, x[4 * i + 2]);
+          sp[3] = fmaf(sp[3], t.w, x[4 * i + 3]);
+        }
+        store_s16(snext, 2 * h2);
+        store_s16(snext, 2 * h2 + 1);
       }
-      ptx::tmem_wait_st();
-      __syncwarp();
+      signal(sready);
       if (lane == 0) ptx::mbar_arrive(&cempty[cs]);
     }
-    if (!failed && warp == 0) bad |= !issue_d2(NT - 1);     // the last chunk's output GEMM
-    if (!failed) failed = ptx::bar_red_or(1, ST_CHAIN, bad);
-    if (failed) {
+    if (!ok) {
       *abort_flag = 1;
-      if (tid == 0) atomicExch(&g_kda_device_error, 1);
+      if (lane == 0) atomicExch(&g_kda_device_error, 1);
     } else {
-      // the last D2 must have landed before TMEM is released (the output warps
-      // wait for it too; this keeps teardown ordered if they gave up early)
       TSO* dst = static_cast<TSO*>(p.state_out) + b * p.so_s[0] + h * p.so_s[1] + v;
 #pragma unroll
       for (int j = 0; j < 64; ++j) st(dst + (int64_t)(64 * hh + j) * p.so_s[2], S[j]);

@@ -12,6 +12,7 @@ translation unit is rebuilt when it or any header under ``csrc/`` or
 
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import os
 import shutil
@@ -61,6 +62,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = Fals
     hdr_mtime = max([os.path.getmtime(h) for h in _headers()] + [0.0])
     objs = []
     relinked = force or not os.path.exists(LIB)
+    jobs = []
     for src in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
         obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
@@ -70,8 +72,13 @@ def build(verbose: bool = False, ptxas_verbose: bool = False, force: bool = Fals
             cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-c", src, "-o", obj]
             if ptxas_verbose:
                 cmd += ["-Xptxas", "-v"]
-            _run(cmd, verbose)
-            relinked = True
+            jobs.append(cmd)
+    if jobs:
+        # translation units compile independently: one nvcc per unit at once
+        with concurrent.futures.ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
+            for f in [ex.submit(_run, cmd, verbose) for cmd in jobs]:
+                f.result()
+        relinked = True
     if relinked or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
         _run([nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], verbose)

@@ -23,7 +23,7 @@
 // Tokens past T are zero rows (q = k = v = g = beta = 0 leave the state and
 // every gradient unchanged).
 //
-// Four kernels, fp32 data; every GEMM runs on the tensor cores as 3xTF32
+// Three kernels, fp32 data; every GEMM runs on the tensor cores as 3xTF32
 // (x = hi + lo, both exact in tf32; hi*hi + hi*lo + lo*hi, ~fp32 accuracy):
 //  * prep_kernel  (b, h, chunk): the pair sums Lraw and Mq as anchored 16-row
 //    block GEMMs (exp(G_ic - G_jc) = exp(G_ic - G_ac) exp(G_ac - G_jc) with the
@@ -31,12 +31,13 @@
 //    channels for which a block is steeper add their exact pair terms
 //    separately), Tinv by forward substitution, KG, Kbar, EQ, GamC -- written
 //    to the per-chunk record;
-//  * fchain_kernel (b, h, 32 state columns): S chunk by chunk (X = KG S,
-//    P = Tinv R, S_next = GamC S + Kbar^T P), storing every chunk-start state
-//    and the chunk's P and Z;
-//  * bchain_kernel (b, h, 32 columns): dS from the end backwards, storing the
-//    gradient of every chunk-end state and dR, writing dv; it needs no S, so
-//    it runs beside fchain on a second stream;
+//  * chains_kernel, two kinds of CTA in one launch:
+//    - forward chain (b, h, 32 state columns): S chunk by chunk (X = KG S,
+//      P = Tinv R, S_next = GamC S + Kbar^T P), storing every chunk-start
+//      state and the chunk's P and Z;
+//    - reverse chain (b, h, 32 columns): dS from the end backwards, storing
+//      the gradient of every chunk-end state and dR, writing dv; it needs no
+//      S, so it runs at the same time as the forward chain;
 //  * grad_kernel  (b, h, chunk): dL, dMq, dEQ, dKG, dKbar from the stored
 //    P, dR, states and dO, the pair terms (the same anchored block GEMMs), and
 //    dq, dk, dg, dbeta (final sums, no partials over V).

@@ -203,7 +203,7 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 // ~1e-6 relative error vanishes in the rounding of SiLU's output to the
 // 16-bit I/O type and is far below the fp32 gates' tolerance.
 constexpr int TTV = 32;   // tokens per tile of the vectorised prologue
-constexpr int NTL = 4;    // tiles per CTA: the next tile's copies fly while this one computes
+constexpr int NTL = 2;    // tiles per CTA: the next tile's copies fly while this one computes
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
@@ -518,7 +518,7 @@ static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
 // accesses, one row per warp).  Same rounding points; the gate's sigmoid uses
 // the fast exponential and divide (~1e-6 relative, below the output's 16-bit
 // rounding).
-constexpr int EPI_ROWS = 8;   // rows per warp of the vectorised epilogue
+constexpr int EPI_ROWS = 4;   // rows per warp of the vectorised epilogue
 
 template <typename TIO>
 __global__ void __launch_bounds__(256)

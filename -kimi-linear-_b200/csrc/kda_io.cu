@@ -24,6 +24,7 @@
 #include <type_traits>
 
 #include "kda_internal.cuh"
+#include "tc_ptx.cuh"
 
 namespace kda {
 namespace io {
@@ -50,6 +51,10 @@ __device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x
 template <typename TIO, typename TG>
 __global__ void __launch_bounds__(128)
 prologue_kernel(const PrologueParams p) {
+  // launched as a programmatic dependent: nothing is touched before the
+  // previous kernel on the stream completed; the next one may start launching
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   __shared__ float ys[TT][128 + 1];
   __shared__ float rstd[TT];
   const int c = threadIdx.x;                       // channel within the head
@@ -284,6 +289,10 @@ __device__ __forceinline__ void stv(T* ptr, const float (&x)[N]) {
 template <typename TIO, typename TG, int HD>
 __global__ void __launch_bounds__(128)
 prologue_vec_kernel(const PrologueParams p) {
+  // launched as a programmatic dependent: nothing is touched before the
+  // previous kernel on the stream completed; the next one may start launching
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   constexpr int CPT = 4, C8 = HD / 8, CG = HD / CPT, TGRP = 128 / CG, TPT = TTV / TGRP;
   static_assert(TPT >= 1 && TPT * TGRP == TTV, "tile split");
   __shared__ __align__(16) TIO xst[2][TTV + 3][HD];   // input rows t0 - 3 .. t0 + TTV - 1
@@ -440,6 +449,10 @@ prologue_vec_kernel(const PrologueParams p) {
 template <typename TIO>
 __global__ void __launch_bounds__(256)
 epilogue_kernel(const EpilogueParams p) {
+  // launched as a programmatic dependent: nothing is touched before the
+  // previous kernel on the stream completed; the next one may start launching
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const long rows = (long)p.B * p.T * p.H;
   if (warp >= rows) return;
@@ -498,16 +511,14 @@ static cudaError_t launch_pro_g(const PrologueParams& p, cudaStream_t s) {
     if (vec_ok(p, sizeof(TG))) {
       const dim3 vgrid((p.T + TTV * NTL - 1) / (TTV * NTL), 4 * p.H, p.B);
       switch (p.K) {
-        case 32: prologue_vec_kernel<TIO, TG, 32><<<vgrid, 128, 0, s>>>(p); break;
-        case 64: prologue_vec_kernel<TIO, TG, 64><<<vgrid, 128, 0, s>>>(p); break;
-        default: prologue_vec_kernel<TIO, TG, 128><<<vgrid, 128, 0, s>>>(p); break;
+        case 32: return launch_dependent(prologue_vec_kernel<TIO, TG, 32>, vgrid, 128, 0, s, p);
+        case 64: return launch_dependent(prologue_vec_kernel<TIO, TG, 64>, vgrid, 128, 0, s, p);
+        default: return launch_dependent(prologue_vec_kernel<TIO, TG, 128>, vgrid, 128, 0, s, p);
       }
-      return cudaGetLastError();
     }
   }
   const int threads = p.K;   // K == V enforced by the caller
-  prologue_kernel<TIO, TG><<<grid, threads, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(prologue_kernel<TIO, TG>, grid, threads, 0, s, p);
 }
 
 // The epilogue for 16-bit I/O with V = 128 and 16-byte-aligned rows: a half
@@ -523,6 +534,10 @@ constexpr int EPI_ROWS = 4;   // rows per warp of the vectorised epilogue
 template <typename TIO>
 __global__ void __launch_bounds__(256)
 epilogue_vec_kernel(const EpilogueParams p) {
+  // launched as a programmatic dependent: nothing is touched before the
+  // previous kernel on the stream completed; the next one may start launching
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   constexpr int NI = EPI_ROWS / 2;
   const long warp = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31, half = lane >> 4, c = lane & 15;
@@ -606,17 +621,15 @@ cudaError_t launch_epilogue(const EpilogueParams& p, cudaStream_t s) {
                    p.y_s[0] % 8 == 0 && p.y_s[1] % 8 == 0;
   const long vblocks = (rows + io::EPI_ROWS * (threads / 32) - 1) / (io::EPI_ROWS * (threads / 32));
   switch (p.io_dtype) {
-    case KDA_DTYPE_F32: io::epilogue_kernel<float><<<blocks, threads, 0, s>>>(p); break;
+    case KDA_DTYPE_F32:
+      return launch_dependent(io::epilogue_kernel<float>, dim3(blocks), threads, 0, s, p);
     case KDA_DTYPE_F16:
-      if (vec) io::epilogue_vec_kernel<__half><<<vblocks, threads, 0, s>>>(p);
-      else io::epilogue_kernel<__half><<<blocks, threads, 0, s>>>(p);
-      break;
+      return vec ? launch_dependent(io::epilogue_vec_kernel<__half>, dim3(vblocks), threads, 0, s, p)
+                 : launch_dependent(io::epilogue_kernel<__half>, dim3(blocks), threads, 0, s, p);
     default:
-      if (vec) io::epilogue_vec_kernel<__nv_bfloat16><<<vblocks, threads, 0, s>>>(p);
-      else io::epilogue_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(p);
-      break;
+      return vec ? launch_dependent(io::epilogue_vec_kernel<__nv_bfloat16>, dim3(vblocks), threads, 0, s, p)
+                 : launch_dependent(io::epilogue_kernel<__nv_bfloat16>, dim3(blocks), threads, 0, s, p);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace kda

@@ -16,6 +16,7 @@
 // registers across all T steps: HBM sees the state read once and written once
 // per launch, which is the whole cost of a decode step (T = 1).
 #include "kda_internal.cuh"
+#include "tc_ptx.cuh"
 
 namespace kda {
 
@@ -47,6 +48,18 @@ recurrent_kernel(const RecParams p) {
   // padded to 16 bytes so the final sums read one float4 per warp and vector
   __shared__ __align__(16) float red[NW][2 * VT + 4];
 
+  // Launched as a programmatic dependent.  The state tile is only prefetched
+  // into L2 before the previous kernel on the stream completed (a prefetch
+  // never returns data, and L2 is where that kernel's writes land, so it is
+  // safe even if that kernel writes the state); every load and store waits.
+  if (FULL) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      ptx::prefetch_l2(static_cast<const TSI*>(p.state_in) + b * p.si_s[0] + h * p.si_s[1] +
+                       (int64_t)(rg + RG * r) * p.si_s[2] + col0);
+  }
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   float S[R][4];
   // ---- load the state tile (zeros when no initial state) -------------------
   const bool vec_s = p.state_vec;
@@ -189,8 +202,7 @@ template <int NTH, int CT, int R, bool FULL, typename TIO, typename TSI, typenam
 static cudaError_t launch_rec(const RecParams& p, cudaStream_t s) {
   constexpr int VT = 4 * CT;
   dim3 grid((p.V + VT - 1) / VT, p.H, p.B);
-  recurrent_kernel<NTH, CT, R, FULL, TIO, TSI, TSO><<<grid, NTH, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(recurrent_kernel<NTH, CT, R, FULL, TIO, TSI, TSO>, grid, NTH, 0, s, p);
 }
 
 #ifndef KDA_REC_FULL_NTH

@@ -183,3 +183,67 @@ def test_module_dropins_prefill_then_decode(cuda_dev):
         xf = o_core * torch.rsqrt(o_core.pow(2).mean(-1, keepdim=True) + 1e-6) * m.g_norm.weight
         ref = m.o_proj((xf * torch.sigmoid(m.og_proj(x).view(2, 33, 2, 64))).reshape(2, 33, 128))
         assert rel(out, ref) < 1e-5
+
+
+def test_decode_chain_in_a_graph_matches_synchronised_calls(cuda_dev):
+    """Three decode steps of one KDA layer at the 1.5B layer shape -- fused
+    prologue from the conv cache, in-place recurrent step, fused epilogue --
+    captured in one CUDA graph, where each kernel is launched as a
+    programmatic dependent of the one before it (it may start before that one
+    finished and must wait before touching its outputs), against the same
+    calls with a device synchronisation after every kernel.  Bit-identical."""
+    kb = pkg()
+    B, H, K, cs = 4, 16, 128, 4
+    D = H * K
+    g = torch.Generator(device=cuda_dev).manual_seed(31)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=cuda_dev) * scale).half()
+
+    steps = [dict(x=[rnd(B, 1, D) for _ in range(4)], beta=rnd(B, 1, H), og=rnd(B, 1, D))
+             for _ in range(3)]
+    w = [(torch.randn(D, 1, cs, generator=g, device=cuda_dev) * 0.4).half().float()
+         for _ in range(3)]
+    bias = [(torch.randn(D, generator=g, device=cuda_dev) * 0.1).half().float() for _ in range(3)]
+    A_log = torch.log(torch.rand(H, K, generator=g, device=cuda_dev) * 15 + 1)
+    dt = torch.log(torch.expm1(torch.rand(H, K, generator=g, device=cuda_dev) * 0.099 + 1e-3))
+    nw = torch.rand(H, K, generator=g, device=cuda_dev) + 0.5
+    hist0 = {n: rnd(B, cs - 1, D) for n in "qkv"}
+    S0 = torch.randn(B, H, K, K, generator=g, device=cuda_dev) * 0.02
+
+    def run(S, sync):
+        hist, outs = hist0, []
+        for st in steps:
+            q, k, v, gg, beta, hist = kb.kda_prologue(*st["x"], st["beta"], w, bias, A_log, dt,
+                                                      H, K, K, 1e-6, conv_cache=hist,
+                                                      want_cache=True)
+            if sync:
+                torch.cuda.synchronize()
+            o, _ = kb.kda_recurrent(q, k, v, gg, beta, state=S, state_dtype=torch.float32,
+                                    inplace=True)
+            if sync:
+                torch.cuda.synchronize()
+            outs.append(kb.kda_epilogue(o, st["og"], nw, 1e-6))
+            if sync:
+                torch.cuda.synchronize()
+        return outs
+
+    S_ref = S0.clone()
+    ref = run(S_ref, True)
+
+    S_g = S0.clone()
+    side = torch.cuda.Stream(cuda_dev)
+    side.wait_stream(torch.cuda.current_stream(cuda_dev))
+    with torch.cuda.stream(side):
+        run(S0.clone(), False)                       # warm-up outside the capture
+    torch.cuda.current_stream(cuda_dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outs = run(S_g, False)
+    S_g.copy_(S0)
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, r in zip(outs, ref):
+        assert torch.equal(a, r)
+    assert torch.equal(S_g, S_ref)
+    assert kb.device_error() == 0

@@ -222,6 +222,37 @@ __device__ __forceinline__ float softplus_fast(float x) {
   return x > 20.f ? x : (u < 0.125f ? ser : lg);
 }
 
+// Two lanes of fp32 arithmetic per instruction (sm_100 FFMA2 / FADD2 / FMUL2,
+// each lane rounded to nearest like the scalar instruction)
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+// a pair rounded to T and back (identity for fp32)
+template <typename T>
+__device__ __forceinline__ float2 rnd2(float2 x) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return __half22float2(__floats2half2_rn(x.x, x.y));
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
+  } else {
+    return x;
+  }
+}
+// softplus_fast of a pair: the series and the final scaling two lanes at a time
+__device__ __forceinline__ float2 softplus2_fast(float2 x) {
+  const float2 u = f2(__expf(x.x), __expf(x.y));
+  const float2 nu = f2(-u.x, -u.y);
+  float2 ser = __ffma2_rn(nu, f2(1.f / 7, 1.f / 7), f2(1.f / 6, 1.f / 6));
+  ser = __ffma2_rn(nu, ser, f2(0.2f, 0.2f));
+  ser = __ffma2_rn(nu, ser, f2(0.25f, 0.25f));
+  ser = __ffma2_rn(nu, ser, f2(1.f / 3, 1.f / 3));
+  ser = __ffma2_rn(nu, ser, f2(0.5f, 0.5f));
+  ser = __ffma2_rn(nu, ser, f2(1.f, 1.f));
+  ser = __fmul2_rn(u, ser);
+  const float2 w = __fadd2_rn(f2(1.f, 1.f), u);
+  const float lx = __logf(w.x), ly = __logf(w.y);
+  return f2(x.x > 20.f ? x.x : (u.x < 0.125f ? ser.x : lx),
+            x.y > 20.f ? x.y : (u.y < 0.125f ? ser.y : ly));
+}
+
 // 16-byte asynchronous copy global -> shared (L2 only); src_bytes = 0 fills zeros
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
@@ -325,7 +356,12 @@ prologue_vec_kernel(const PrologueParams p) {
       if (i0 + i >= nt) break;
       float y[CPT];
 #pragma unroll
-      for (int e = 0; e < CPT; ++e) y[e] = a[e] * softplus_fast(gv[i][e] + dtb[e]);
+      for (int e = 0; e < CPT; e += 2) {
+        const float2 sp = softplus2_fast(__fadd2_rn(f2(gv[i][e], gv[i][e + 1]), f2(dtb[e], dtb[e + 1])));
+        const float2 r = __fmul2_rn(f2(a[e], a[e + 1]), sp);
+        y[e] = r.x;
+        y[e + 1] = r.y;
+      }
       stv<CPT>(g + (int64_t)(t0 + i0 + i) * p.g_s[1], y);
     }
     for (int i = tid; i < nt; i += blockDim.x) {       // beta: every token of the tile
@@ -353,21 +389,29 @@ prologue_vec_kernel(const PrologueParams p) {
   // rows outside the input and the history are zero-filled)
   const TIO* xh = x - CPT * cg;                      // channel 0 of this head
   const TIO* hh = hb ? hb - CPT * cg : nullptr;
+  // A thread copies the same 16-byte column c8 of every (128 / C8)-th row, so
+  // its source and destination advance by constant strides.
   auto stage = [&](int k) {
+    constexpr int RS = 128 / C8;                   // rows per pass of the CTA
+    static_assert(RS * C8 == 128, "whole rows per pass");
     const int t0 = (tile0 + k) * TTV, nt = min(TTV, p.T - t0);
-    for (int q = tid; q < (TTV + 3) * C8; q += 128) {
-      const int row = q / C8, c8 = q - row * C8;
+    const int c8 = tid % C8;
+    int row = tid / C8;
+    int64_t off = (int64_t)(t0 + row - 3) * xs + 8 * c8;   // element offset of row's input
+    const int64_t step = (int64_t)RS * xs;
+    TIO* dst = &xst[k & 1][row][8 * c8];
+    for (; row < TTV + 3; row += RS, off += step, dst += RS * HD) {
       const int i = row - 3, t = t0 + i;
       const TIO* src = xh;
       uint32_t bytes = 0;
       if (i < nt && t >= 0) {
-        src = xh + (int64_t)t * xs + 8 * c8;
+        src = xh + off;
         bytes = 16;
       } else if (i < nt && hh != nullptr && t >= -keep) {
         src = hh + (int64_t)(keep + t) * D + 8 * c8;
         bytes = 16;
       }
-      cp_async16(&xst[k & 1][row][8 * c8], src, bytes);
+      cp_async16(dst, src, bytes);
     }
   };
   stage(0);
@@ -397,6 +441,7 @@ prologue_vec_kernel(const PrologueParams p) {
   // norm is a shuffle reduction (rows past nt are zeros and are not stored).
   {
     const TIO* xb = &xst[k & 1][i0][CPT * cg];
+    TIO* orow = out + (int64_t)(t0 + i0) * os;       // output row of token i0 + i
     float xw[4][CPT];
 #pragma unroll
     for (int j = 0; j < 3; ++j) ldv<CPT>(xb + j * HD, xw[j + 1]);
@@ -407,24 +452,37 @@ prologue_vec_kernel(const PrologueParams p) {
 #pragma unroll
         for (int e = 0; e < CPT; ++e) xw[j][e] = xw[j + 1][e];
       ldv<CPT>(xb + (i + 3) * HD, xw[3]);
-      float y[CPT], ss = 0.f;
+      // two channels per instruction: conv, the SiLU denominator, the squares
+      float y[CPT];
+      float2 ss2 = f2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < CPT; ++e) {
-        float acc = bv[e];
+      for (int e = 0; e < CPT; e += 2) {
+        float2 acc = f2(bv[e], bv[e + 1]);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          if (j >= 4 - cs) acc = fmaf(xw[j][e], wv[e][j], acc);
-        y[e] = rnd<TIO>(silu_fast(rnd<TIO>(acc)));
-        ss = fmaf(y[e], y[e], ss);
+          if (j >= 4 - cs)
+            acc = __ffma2_rn(f2(xw[j][e], xw[j][e + 1]), f2(wv[e][j], wv[e + 1][j]), acc);
+        const float2 c = rnd2<TIO>(acc);
+        const float2 den = __fadd2_rn(f2(1.f, 1.f), f2(__expf(-c.x), __expf(-c.y)));
+        const float2 sv = rnd2<TIO>(f2(__fdividef(c.x, den.x), __fdividef(c.y, den.y)));
+        ss2 = __ffma2_rn(sv, sv, ss2);
+        y[e] = sv.x;
+        y[e + 1] = sv.y;
       }
       if (norm) {
+        float ss = ss2.x + ss2.y;
 #pragma unroll
         for (int off = 1; off < CG; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float r = fminf(rsqrtf(ss), 1.f / p.eps);
 #pragma unroll
-        for (int e = 0; e < CPT; ++e) y[e] *= r;
+        for (int e = 0; e < CPT; e += 2) {
+          const float2 sc = __fmul2_rn(f2(y[e], y[e + 1]), f2(r, r));
+          y[e] = sc.x;
+          y[e + 1] = sc.y;
+        }
       }
-      if (i0 + i < nt) stv<CPT>(out + (int64_t)(t0 + i0 + i) * os, y);
+      if (i0 + i < nt) stv<CPT>(orow, y);
+      orow += os;
     }
   }
   // new conv cache: the last keep inputs of cat(history, x)

@@ -348,9 +348,11 @@ prologue_vec_kernel(const PrologueParams p) {
     const int t0 = (tile0 + k) * TTV;
     const int nt = min(TTV, p.T - t0);
     float gv[TPT][CPT];
+    const TG* grow = gk + (int64_t)(t0 + i0) * p.gk_s[1];   // input row of token i0 + i
+    float* orow = g + (int64_t)(t0 + i0) * p.g_s[1];        // output row of token i0 + i
 #pragma unroll
     for (int i = 0; i < TPT; ++i)
-      if (i0 + i < nt) ldv<CPT>(gk + (int64_t)(t0 + i0 + i) * p.gk_s[1], gv[i]);
+      if (i0 + i < nt) ldv<CPT>(grow + i * p.gk_s[1], gv[i]);
 #pragma unroll
     for (int i = 0; i < TPT; ++i) {
       if (i0 + i >= nt) break;
@@ -362,7 +364,8 @@ prologue_vec_kernel(const PrologueParams p) {
         y[e] = r.x;
         y[e + 1] = r.y;
       }
-      stv<CPT>(g + (int64_t)(t0 + i0 + i) * p.g_s[1], y);
+      stv<CPT>(orow, y);
+      orow += p.g_s[1];
     }
     for (int i = tid; i < nt; i += blockDim.x) {       // beta: every token of the tile
       const int t = t0 + i;

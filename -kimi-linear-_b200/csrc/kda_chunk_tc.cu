@@ -513,12 +513,13 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
     float2 ra[8], nb[8];
     if (hf == 1 && r == 3) al[8] = make_float2(1.f, 1.f);
     ra[0] = hf ? make_float2(__expf(ox), __expf(oy)) : make_float2(1.f, 1.f);
+    // channel pairs as two-lane fp32 multiplies (each lane rounded like a
+    // scalar multiply, so the values are those of the scalar code)
 #pragma unroll
-    for (int i = 1; i < 8; ++i) ra[i] = make_float2(ra[i - 1].x * al[i].x, ra[i - 1].y * al[i].y);
-    nb[7] = hf ? al[8] : make_float2(al[8].x * __expf(ox), al[8].y * __expf(oy));
+    for (int i = 1; i < 8; ++i) ra[i] = __fmul2_rn(ra[i - 1], al[i]);
+    nb[7] = hf ? al[8] : __fmul2_rn(al[8], make_float2(__expf(ox), __expf(oy)));
 #pragma unroll
-    for (int i = 6; i >= 0; --i)
-      nb[i] = make_float2(nb[i + 1].x * al[i + 1].x, nb[i + 1].y * al[i + 1].y);
+    for (int i = 6; i >= 0; --i) nb[i] = __fmul2_rn(nb[i + 1], al[i + 1]);
     // Qbar, Ktilde and V go out as 16-byte core-matrix rows: the four lanes of
     // a quad hold the four channel pairs of one 8-channel group, so after a
     // quad transpose of four rows each lane owns one whole row of the group.
@@ -529,14 +530,15 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
       for (int ii = 0; ii < 4; ++ii) {
         const int i = i4 + ii, c = rb0 + i;
         const float2 qv = qr[i], kv = kr[i], vv = vr[i];
-        const float qsx = qv.x * s, qsy = qv.y * s;
-        const float egx = bfx * ra[i].x, egy = bfy * ra[i].y;   // exp(gc_c)
-        qh[ii] = pack_h2(qsx * egx, qsy * egy);                  // Qbar (-> E later)
-        kh[ii] = pack_h2(kv.x * egx, kv.y * egy);                // Ktilde (-> -W later)
+        const float2 qs = __fmul2_rn(qv, make_float2(s, s));
+        const float2 eg = __fmul2_rn(make_float2(bfx, bfy), ra[i]);   // exp(gc_c)
+        const float2 qb2 = __fmul2_rn(qs, eg), kt2 = __fmul2_rn(kv, eg);
+        qh[ii] = pack_h2(qb2.x, qb2.y);                          // Qbar (-> E later)
+        kh[ii] = pack_h2(kt2.x, kt2.y);                          // Ktilde (-> -W later)
         vh[ii] = pack_h2(vv.x, vv.y);                            // V (-> U later)
-        *reinterpret_cast<float2*>(Axk + c * AXP + k0) = make_float2(kv.x * ra[i].x, kv.y * ra[i].y);
-        *reinterpret_cast<float2*>(Axq + c * AXP + k0) = make_float2(qsx * ra[i].x, qsy * ra[i].y);
-        *reinterpret_cast<float2*>(Yb + c * AXP + k0) = make_float2(kv.x * nb[i].x, kv.y * nb[i].y);
+        *reinterpret_cast<float2*>(Axk + c * AXP + k0) = __fmul2_rn(kv, ra[i]);
+        *reinterpret_cast<float2*>(Axq + c * AXP + k0) = __fmul2_rn(qs, ra[i]);
+        *reinterpret_cast<float2*>(Yb + c * AXP + k0) = __fmul2_rn(kv, nb[i]);
       }
       quad_transpose(qh, tig);
       quad_transpose(kh, tig);
@@ -607,8 +609,10 @@ prep_kernel(const ChunkParams p, uint8_t* __restrict__ ws, unsigned int* __restr
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const float4 y = *reinterpret_cast<const float4*>(Yb + (16 * j + 8 * nt + gid) * AXP + kc);
-          const uint32_t b0[2] = {ptx::f32_to_tf32(y.x * fv.x), ptx::f32_to_tf32(y.y * fv.y)};
-          const uint32_t b1[2] = {ptx::f32_to_tf32(y.z * fv.z), ptx::f32_to_tf32(y.w * fv.w)};
+          const float2 yf0 = __fmul2_rn(make_float2(y.x, y.y), make_float2(fv.x, fv.y));
+          const float2 yf1 = __fmul2_rn(make_float2(y.z, y.w), make_float2(fv.z, fv.w));
+          const uint32_t b0[2] = {ptx::f32_to_tf32(yf0.x), ptx::f32_to_tf32(yf0.y)};
+          const uint32_t b1[2] = {ptx::f32_to_tf32(yf1.x), ptx::f32_to_tf32(yf1.y)};
           ptx::mma_tf32_16x8x8(acc2[g & 1][nt], af[g][0], b0);
           ptx::mma_tf32_16x8x8(acc2[g & 1][nt], af[g][1], b1);
         }

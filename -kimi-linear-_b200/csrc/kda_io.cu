@@ -208,7 +208,7 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 // ~1e-6 relative error vanishes in the rounding of SiLU's output to the
 // 16-bit I/O type and is far below the fp32 gates' tolerance.
 constexpr int TTV = 32;   // tokens per tile of the vectorised prologue
-constexpr int NTL = 2;    // tiles per CTA: the next tile's copies fly while this one computes
+constexpr int NTL = 3;    // tiles per CTA: the next tile's copies fly while this one computes
 
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }

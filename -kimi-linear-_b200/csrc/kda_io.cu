@@ -203,7 +203,10 @@ __device__ __forceinline__ void st8v(T* ptr, const float (&x)[8]) {
 // 0.6 TB/s.  Tiles of TTV = 32 tokens; 4 channels a thread keep the conv taps
 // in 16 registers (80 a thread, six CTAs an SM).  The grid's y index
 // interleaves the four tensors (q, k, v, gates) head by head, so the cheaper
-// gate CTAs do not all land in the last wave.  Same rounding points; SiLU,
+// gate CTAs do not all land in the last wave.  A thread's channels are
+// computed in pairs with the two-lane fp32 instructions of sm_100 (FFMA2 /
+// FADD2 / FMUL2, each lane rounded like the scalar instruction): the kernel
+// is issue-bound.  Same rounding points; SiLU,
 // sigmoid and softplus use the fast exponential, logarithm and divide, whose
 // ~1e-6 relative error vanishes in the rounding of SiLU's output to the
 // 16-bit I/O type and is far below the fp32 gates' tolerance.

@@ -111,11 +111,19 @@ recurrent_kernel(const RecParams p) {
       if (FULL || i < K) {
         const float al = sa[buf][i], kk = sk[buf][i], qq = sq[buf][i];
         qk = fmaf(qq, kk, qk);
+        // column pairs as two-lane fp32 instructions (each lane rounded like
+        // the scalar instruction, so the values are those of the scalar code)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          S[r][c] *= al;
-          a[c] = fmaf(kk, S[r][c], a[c]);
-          bq[c] = fmaf(qq, S[r][c], bq[c]);
+        for (int c = 0; c < 4; c += 2) {
+          const float2 s2 = __fmul2_rn(make_float2(S[r][c], S[r][c + 1]), make_float2(al, al));
+          const float2 a2 = __ffma2_rn(make_float2(kk, kk), s2, make_float2(a[c], a[c + 1]));
+          const float2 b2 = __ffma2_rn(make_float2(qq, qq), s2, make_float2(bq[c], bq[c + 1]));
+          S[r][c] = s2.x;
+          S[r][c + 1] = s2.y;
+          a[c] = a2.x;
+          a[c + 1] = a2.y;
+          bq[c] = b2.x;
+          bq[c + 1] = b2.y;
         }
       }
     }
@@ -162,7 +170,12 @@ recurrent_kernel(const RecParams p) {
       if (FULL || i < K) {
         const float kk = sk[buf][i];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) S[r][c] = fmaf(kk, u[c], S[r][c]);
+        for (int c = 0; c < 4; c += 2) {
+          const float2 s2 = __ffma2_rn(make_float2(kk, kk), make_float2(u[c], u[c + 1]),
+                                       make_float2(S[r][c], S[r][c + 1]));
+          S[r][c] = s2.x;
+          S[r][c + 1] = s2.y;
+        }
       }
     }
     if (rg == 0) {
